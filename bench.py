@@ -1,0 +1,434 @@
+"""Benchmark of the fpscan hot path on B200 (one process per GPU).
+
+Default workload: pscan forward + backward, bf16,
+batch 16 x dim 5120 x seqlen 16384, gates = exp(-softplus(z)), z ~ N(-1,1),
+tokens, grad_out ~ N(0,1), seeded; the 81920 channels are split evenly over
+the N ranks (fixed total work: strong scaling) with no communication.
+A step is one PScan forward + backward (two kernels: scan, fused backward).
+
+Metric: algorithmic HBM bytes / time, aggregated over all ranks, in GB/s:
+3*N*s forward + 5*N*s backward (s = element size).  Every tensor is far
+larger than L2 (126 MB), so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME]
+    python bench.py --impl reference     # the reference's CPU path, timed on the host
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "scan HBM GB/s (% of B200 peak) and fwd+bwd p50 ms at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+CONFIGS = {
+    # channel-sharded bf16 fwd+bwd
+    "shard_bd": dict(batch=16, dim=5120, seqlen=16384, dtype="bfloat16", gates="exp_softplus",
+                     tokens_scale="unit"),
+    # Mamba-like half fwd+bwd (single GPU, or channel-sharded)
+    "halfbwd_bf16": dict(batch=8, dim=2048, seqlen=8192, dtype="bfloat16", gates="sigmoid",
+                         tokens_scale="0.1"),
+    "halfbwd_fp16": dict(batch=8, dim=2048, seqlen=8192, dtype="float16", gates="sigmoid",
+                         tokens_scale="0.1"),
+}
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the backward
+# kernel from ncu (profiles/scan_bwd_bf16_cfg4.md); None until captured.
+NCU_TRAFFIC_BYTES = {}
+
+
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.proc = None
+        self.out = None
+        bus = None
+        try:
+            p = torch.cuda.get_device_properties(device)
+            bus = "%08X:%02X:%02X.0" % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+        except Exception:
+            pass
+        self.cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                    "-lms", "200"] + ([f"--id={bus}"] if bus else [])
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [s.strip() for s in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _make_inputs(cfg, rows_lo, rows_hi, device, seed=0):
+    """This rank's rows of the config's synthetic inputs (seeded per rank slice)."""
+    dtype = getattr(torch, cfg["dtype"])
+    L = cfg["seqlen"]
+    n = rows_hi - rows_lo
+    gen = torch.Generator(device=device).manual_seed(seed * 1000003 + rows_lo)
+    shape = (1, n, L)
+    z = torch.randn(shape, generator=gen, device=device)
+    if cfg["gates"] == "exp_softplus":
+        gates = torch.exp(-torch.nn.functional.softplus(z - 1.0)).to(dtype)
+    else:
+        gates = torch.sigmoid(z + 2.0).to(dtype)
+    del z
+    scale = 0.1 if cfg["tokens_scale"] == "0.1" else 1.0
+    tokens = (torch.randn(shape, generator=gen, device=device) * scale).to(dtype)
+    grad_out = torch.randn(shape, generator=gen, device=device).to(dtype)
+    return gates, tokens, grad_out
+
+
+def _cpu_baseline(cfg, target_s=8.0):
+    """Serial fp32 oracle (forward + fused backward), all host threads, on a
+    bounded sample of the workload's rows, repeated for about target_s;
+    GB/s by the same byte formula as the GPU line."""
+    import oracle
+
+    L = cfg["seqlen"]
+    rows_total = cfg["batch"] * cfg["dim"]
+    s = torch.empty((), dtype=getattr(torch, cfg["dtype"])).element_size()
+    rng = np.random.default_rng(0)
+
+    def make(rows):
+        # gates in (0.27, 1) like exp(-softplus(N(-1,1))); timing does not
+        # depend on the exact distribution
+        g = (0.27 + 0.73 * rng.random((rows, L), dtype=np.float32)).astype(np.float32)
+        x = rng.random((rows, L), dtype=np.float32) - 0.5
+        go = rng.random((rows, L), dtype=np.float32) - 0.5
+        return g, x, go
+
+    rows = min(rows_total, 4096)
+    g, x, go = make(rows)
+    oracle.pscan_fwdbwd_f32(g, x, go)  # warm-up (first touch of the outputs)
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.pscan_fwdbwd_f32(g, x, go)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= target_s:
+            break
+    rows_done = rows * reps
+    return {"value": round(8 * rows_done * L * s / dt / 1e9, 3), "unit": "GB/s",
+            "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{rows} of {rows_total} rows x {L}, {reps} passes, fp32 serial forward + "
+                      f"fused backward (oracle/scan_oracle.c, OpenMP over rows), {dt:.2f} s"}
+
+
+def run_reference(args, cfg):
+    """The reference's own CPU implementation of the path: parallel_scan_torch
+    (Hillis-Steele, eval/baselines.py:40-61, restated in oracle/) forward plus
+    torch autograd backward, all host threads, on a bounded sample of rows."""
+    world, rank, _ = _dist_env()
+    if rank != 0:
+        return
+    import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    dtype = getattr(torch, cfg["dtype"])
+    L = cfg["seqlen"]
+    s = torch.empty((), dtype=dtype).element_size()
+    gen = torch.Generator().manual_seed(0)
+
+    def make(rows):
+        z = torch.randn(1, rows, L, generator=gen)
+        g = torch.exp(-torch.nn.functional.softplus(z - 1.0)).to(dtype).requires_grad_()
+        x = torch.randn(1, rows, L, generator=gen).to(dtype).requires_grad_()
+        go = torch.randn(1, rows, L, generator=gen).to(dtype)
+        return g, x, go
+
+    def step(g, x, go):
+        y = oracle.parallel_scan_torch(g, x)
+        torch.autograd.grad(y, (g, x), go)
+
+    # size the per-step sample so the whole run stays within a few minutes
+    rows = 8
+    while True:
+        g, x, go = make(rows)
+        t0 = time.perf_counter()
+        step(g, x, go)
+        dt = time.perf_counter() - t0
+        if dt * 2 * (args.steps + args.warmup) > 120 or rows >= 8192:
+            break
+        rows *= 2
+    g, x, go = make(rows)
+    for _ in range(args.warmup):
+        step(g, x, go)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step(g, x, go)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = 8 * rows * L * s * args.steps / total / 1e9
+    sample = (f"{rows} of {cfg['batch'] * cfg['dim']} rows x {L} {cfg['dtype']} per step, "
+              f"parallel_scan_torch forward + autograd backward on CPU")
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
+        "config": _config_json(args, cfg, world),
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s",
+                         "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _config_json(args, cfg, world):
+    return {"workload": f"{args.config}: pscan fwd+bwd {cfg['dtype']} batch={cfg['batch']} "
+                        f"dim={cfg['dim']} seqlen={cfg['seqlen']}, channels split over {world} GPU(s)",
+            "batch": cfg["batch"], "dim": cfg["dim"], "seqlen": cfg["seqlen"],
+            "parallelism": f"channel-shard x{world}",
+            "l2": "inputs larger than L2 (no flush)"}
+
+
+def run_fpscan(args, cfg):
+    import torch.distributed as dist
+
+    import fpscan_b200
+    from fpscan_b200 import _lib
+    from fpscan_b200.distributed import channel_slice
+
+    world, rank, local = _dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    _lib.load()
+
+    rows_total = cfg["batch"] * cfg["dim"]
+    lo, hi = channel_slice(rows_total, rank, world)
+    L = cfg["seqlen"]
+    dtype = getattr(torch, cfg["dtype"])
+    s = torch.empty((), dtype=dtype).element_size()
+    gates, tokens, grad_out = _make_inputs(cfg, lo, hi, device)
+    gates.requires_grad_()
+    tokens.requires_grad_()
+    n_local = (hi - lo) * L
+
+    def step():
+        y = fpscan_b200.pscan(gates, tokens)
+        torch.autograd.grad(y, (gates, tokens), grad_out)
+
+    stream = torch.cuda.current_stream(device)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(local) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        y = fpscan_b200.pscan(gates, tokens)
+        ev[i][1].record(stream)
+        torch.autograd.grad(y, (gates, tokens), grad_out)
+        ev[i][2].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clock_info = clocks.stop() if clocks else None
+    elapsed_ms = t_start.elapsed_time(t_end)
+    fwd_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    bwd_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    step_ms = [e[0].elapsed_time(e[2]) for e in ev]
+
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item())
+    total_bytes = 8 * rows_total * L * s * args.steps
+    value = total_bytes / (max_ms / 1e3) / 1e9
+
+    peak, peak_kind = _peaks()
+    bwd_mean = statistics.mean(bwd_ms)
+    fwd_mean = statistics.mean(fwd_ms)
+    achieved_bwd = 5 * n_local * s / (bwd_mean / 1e3) / 1e9
+    achieved_fwd = 3 * n_local * s / (fwd_mean / 1e3) / 1e9
+    traffic = NCU_TRAFFIC_BYTES.get((args.config, world))
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = _e2e(args, cfg, gates.detach(), tokens.detach(), grad_out, device, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = _cpu_baseline(cfg)
+
+    status = _lib.device_status()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": cfg["dtype"],
+            "data": "synthetic (seeded; BASELINE config distributions)",
+            "config": _config_json(args, cfg, world),
+            "pct_of_hbm_peak": round(100 * value / world / peak, 2),
+            "fwd_bwd_p50_ms": round(statistics.median(step_ms), 4),
+            "fwd_p50_ms": round(statistics.median(fwd_ms), 4),
+            "bwd_p50_ms": round(statistics.median(bwd_ms), 4),
+            "fwd_achieved_gbs": round(achieved_fwd, 1),
+            "roofline": {"bound": "hbm", "kernel": "scan_bwd_kernel (fused backward)",
+                         "achieved": round(achieved_bwd, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved_bwd / peak, 4), "peak_source": peak_kind,
+                         "traffic": traffic,
+                         "algorithmic_bytes_per_launch": 5 * n_local * s},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clock_info,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _e2e(args, cfg, gates_d, tokens_d, grad_out_d, device, world):
+    """Same metric through the public API with host (pinned) buffers: every
+    step copies this step's inputs host->device and all results back."""
+    import torch.distributed as dist
+
+    import fpscan_b200
+
+    g_h = gates_d.cpu().pin_memory()
+    x_h = tokens_d.cpu().pin_memory()
+    go_h = grad_out_d.cpu().pin_memory()
+    y_h = torch.empty_like(g_h).pin_memory()
+    dg_h = torch.empty_like(g_h).pin_memory()
+    dt_h = torch.empty_like(g_h).pin_memory()
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        g = g_h.to(device, non_blocking=True).requires_grad_()
+        x = x_h.to(device, non_blocking=True).requires_grad_()
+        go = go_h.to(device, non_blocking=True)
+        y = fpscan_b200.pscan(g, x)
+        dg, dt = torch.autograd.grad(y, (g, x), go)
+        y_h.copy_(y.detach(), non_blocking=True)
+        dg_h.copy_(dg, non_blocking=True)
+        dt_h.copy_(dt, non_blocking=True)
+
+    step()
+    torch.cuda.synchronize()
+    k = max(1, min(args.steps, args.e2e_steps))
+    if world > 1:
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(k):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    L = cfg["seqlen"]
+    s = g_h.element_size()
+    rows_total = cfg["batch"] * cfg["dim"]
+    value = 8 * rows_total * L * s * k / (float(t.item()) / 1e3) / 1e9
+    nbytes = g_h.numel() * s
+    return {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 3 * nbytes,
+            "d2h_bytes_per_step": 3 * nbytes, "steps": k,
+            "path": "pinned host -> fpscan_b200.pscan fwd+bwd -> pinned host, one stream"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["fpscan", "reference"], default="fpscan")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="shard_bd")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_fpscan(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,83 @@
+"""ctypes binding of ``libfpscan_b200.so`` (the C ABI in include/fpscan_b200.h).
+
+The shared object is built in-tree by ``python -m fpscan_b200.build``.  There
+is no fallback: if the library is missing or fails to load, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+LIB_PATH = _build.LIB_PATH
+
+_c_i64 = ctypes.c_int64
+_c_int = ctypes.c_int
+_vp = ctypes.c_void_p
+
+# name -> argtypes, every function returns int except fpscan_last_error.
+SIGNATURES = {
+    "fpscan_abi_version": [],
+    "fpscan_scan_fwd": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
+    "fpscan_scan_bwd": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
+    "fpscan_shard_fwd_reduce": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
+    "fpscan_shard_fwd_scan": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
+    "fpscan_shard_bwd_reduce": [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
+    "fpscan_shard_bwd_scan": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
+    "fpscan_carry_combine": [_vp, _c_int, _c_int, _c_i64, _c_int, _vp, _vp],
+    "fpscan_last_error": [],
+    "fpscan_device_status": [ctypes.POINTER(ctypes.c_uint), _c_int],
+}
+
+EXPECTED_ABI_VERSION = 1
+
+_lock = threading.Lock()
+_lib = None
+
+
+class FpscanError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once (thread-safe) and set up its signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"fpscan_b200 CUDA library not found at {LIB_PATH}; build it with "
+                "`python -m fpscan_b200.build` (needs nvcc for sm_100a)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_char_p if name == "fpscan_last_error" else ctypes.c_int
+        ver = lib.fpscan_abi_version()
+        if ver != EXPECTED_ABI_VERSION:
+            raise ImportError(f"libfpscan_b200 ABI version {ver}, expected {EXPECTED_ABI_VERSION}")
+        _lib = lib
+        return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().fpscan_last_error().decode(errors="replace")
+        raise FpscanError(f"{what}: {msg}")
+
+
+def call(name: str, *args) -> None:
+    lib = load()
+    check(getattr(lib, name)(*args), name)
+
+
+def device_status(clear: bool = True) -> int:
+    """Synchronously read the current device's status word (0 = healthy)."""
+    v = ctypes.c_uint(0)
+    check(load().fpscan_device_status(ctypes.byref(v), 1 if clear else 0), "fpscan_device_status")
+    return int(v.value)

@@ -1,0 +1,97 @@
+"""Build libfpscan_b200.so in-tree with nvcc for sm_100a.
+
+The library is a plain C-ABI shared object (no torch / pybind dependency):
+every ``csrc/*.cu`` is compiled with relocatable device code (the device
+status word is shared between translation units) and linked with the CUDA
+runtime statically.  Rebuilds only when a source or header is newer than the
+library.  Usage: ``python -m fpscan_b200.build [--force]``.
+"""
+from __future__ import annotations
+
+import glob
+import os
+import subprocess
+import sys
+import tempfile
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+REPO_DIR = os.path.dirname(PKG_DIR)
+CSRC = os.path.join(PKG_DIR, "csrc")
+LIB_NAME = "libfpscan_b200.so"
+LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "-rdc=true",
+    "-Xcompiler", "-fPIC",
+    "-Xcompiler", "-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+]
+
+
+def _nvcc() -> str:
+    cand = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
+    return cand if os.path.exists(cand) else "nvcc"
+
+
+def _sources():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+
+
+def _deps():
+    return (_sources() + glob.glob(os.path.join(CSRC, "*.cuh"))
+            + glob.glob(os.path.join(CSRC, "*.h"))
+            + glob.glob(os.path.join(REPO_DIR, "include", "*.h")) + [__file__])
+
+
+def needs_build() -> bool:
+    if not os.path.exists(LIB_PATH):
+        return True
+    t = os.path.getmtime(LIB_PATH)
+    return any(os.path.getmtime(p) > t for p in _deps())
+
+
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> str:
+    """Compile the library if needed; returns its path."""
+    if not force and not needs_build():
+        return LIB_PATH
+    nvcc = _nvcc()
+    extra = ["-Xptxas", "-v"] if ptxas_verbose else []
+    with tempfile.TemporaryDirectory(prefix="fpscan_build_") as tmp:
+        objs = []
+        procs = []
+        for src in _sources():
+            obj = os.path.join(tmp, os.path.basename(src) + ".o")
+            cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, *extra, "-I", CSRC,
+                   "-I", os.path.join(REPO_DIR, "include"), "-c", src, "-o", obj]
+            if verbose:
+                print(" ".join(cmd))
+            procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE,
+                                                stderr=subprocess.STDOUT, text=True)))
+            objs.append(obj)
+        failed = []
+        for src, p in procs:
+            out, _ = p.communicate()
+            if out and (verbose or ptxas_verbose or p.returncode):
+                print(out, file=sys.stderr)
+            if p.returncode:
+                failed.append(src)
+        if failed:
+            raise RuntimeError(f"nvcc failed for {failed}")
+        tmp_lib = os.path.join(tmp, LIB_NAME)
+        cmd = [nvcc, *ARCH_FLAGS, "-rdc=true", "-shared", "-Xcompiler", "-fPIC",
+               *objs, "-o", tmp_lib]
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+        os.replace(tmp_lib, LIB_PATH)
+    return LIB_PATH
+
+
+if __name__ == "__main__":
+    path = build(force="--force" in sys.argv, verbose="-v" in sys.argv,
+                 ptxas_verbose="--ptxas" in sys.argv)
+    print(path)

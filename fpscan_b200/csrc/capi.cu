@@ -1,0 +1,263 @@
+// C-ABI entry points (include/fpscan_b200.h): argument validation, dispatch
+// and error reporting.  The reference performs its checks with TORCH_CHECK
+// (csrc/full_scan/full_scan.h:7-15, csrc/full_scan/full_scan.cu:181-182,
+// 232, 240-256); here the same conditions, plus the ones it omits (output
+// shape/alignment, aliasing, launch errors), produce FPSCAN_ERR_* codes with a
+// message in fpscan_last_error().
+#include "../../include/fpscan_b200.h"
+#include "common.cuh"
+#include "internal.h"
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+namespace fpscan {
+
+__device__ unsigned int g_status = 0;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int ok() {
+  t_last_error.clear();
+  return FPSCAN_OK;
+}
+
+bool is_pow2(int64_t v) { return v > 0 && (v & (v - 1)) == 0; }
+
+int num_sms_current() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < 64) {
+    int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    sms = 148;
+  if (dev >= 0 && dev < 64) cache[dev].store(sms, std::memory_order_relaxed);
+  return sms;
+}
+
+struct Span {
+  const char* name;
+  uintptr_t lo, hi;
+};
+
+bool overlaps(const Span& a, const Span& b) { return a.lo < b.hi && b.lo < a.hi; }
+
+int check_dtype(int dtype) {
+  if (dtype != kF32 && dtype != kF16 && dtype != kBF16)
+    return fail(FPSCAN_ERR_INVALID,
+                "unsupported dtype code %d: expecting float32 (0), float16 (1) or bfloat16 (2)",
+                dtype);
+  return FPSCAN_OK;
+}
+
+int check_ptr(const void* p, const char* name) {
+  if (p == nullptr) return fail(FPSCAN_ERR_INVALID, "%s is NULL", name);
+  if (reinterpret_cast<uintptr_t>(p) % 16 != 0)
+    return fail(FPSCAN_ERR_INVALID, "%s must be 16-byte aligned", name);
+  return FPSCAN_OK;
+}
+
+// rows = batch*dim, with overflow and sign checks.
+int check_shape(int64_t batch, int64_t dim, int64_t seqlen, int64_t min_l, int64_t max_l,
+                int64_t* rows) {
+  if (batch < 0 || dim < 0)
+    return fail(FPSCAN_ERR_INVALID, "batch (%lld) and dim (%lld) must be non-negative",
+                (long long)batch, (long long)dim);
+  if (!is_pow2(seqlen) || seqlen < min_l || seqlen > max_l)
+    return fail(FPSCAN_ERR_INVALID, "seqlen must be a power of 2, >= %lld, <= %lld (got %lld)",
+                (long long)min_l, (long long)max_l, (long long)seqlen);
+  if (dim != 0 && batch > INT64_MAX / dim)
+    return fail(FPSCAN_ERR_INVALID, "batch*dim overflows");
+  const int64_t r = batch * dim;
+  if (r != 0 && r > INT64_MAX / seqlen / 4)
+    return fail(FPSCAN_ERR_INVALID, "tensor too large");
+  if (r > (int64_t)0x7fffffff * 64)
+    return fail(FPSCAN_ERR_INVALID, "batch*dim too large for the launch grid");
+  *rows = r;
+  return FPSCAN_OK;
+}
+
+int cuda_result(cudaError_t e, const char* what) {
+  if (e != cudaSuccess)
+    return fail(FPSCAN_ERR_CUDA, "%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
+  return ok();
+}
+
+constexpr int64_t kRefMinL = 32, kRefMaxL = 65536;  // csrc/full_scan/full_scan.cu:207-233
+constexpr int64_t kShardMaxL = int64_t(1) << 24;
+
+#define FPSCAN_TRY(expr)          \
+  do {                            \
+    int _rc = (expr);             \
+    if (_rc != FPSCAN_OK) return _rc; \
+  } while (0)
+
+}  // namespace
+}  // namespace fpscan
+
+using namespace fpscan;
+
+extern "C" {
+
+int fpscan_abi_version(void) { return FPSCAN_ABI_VERSION; }
+
+const char* fpscan_last_error(void) { return t_last_error.c_str(); }
+
+int fpscan_scan_fwd(const void* gates, const void* tokens, void* out, int64_t batch, int64_t dim,
+                    int64_t seqlen, int dtype, int reverse, void* stream) {
+  int64_t rows = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape(batch, dim, seqlen, kRefMinL, kRefMaxL, &rows));
+  if (rows == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(tokens, "tokens"));
+  FPSCAN_TRY(check_ptr(out, "out"));
+  const uintptr_t bytes = (uintptr_t)(rows * seqlen * dtype_size(dtype));
+  const Span so{"out", (uintptr_t)out, (uintptr_t)out + bytes};
+  const Span sg{"gates", (uintptr_t)gates, (uintptr_t)gates + bytes};
+  const Span st{"tokens", (uintptr_t)tokens, (uintptr_t)tokens + bytes};
+  for (const Span* in : {&sg, &st})
+    if (overlaps(so, *in) && so.lo != in->lo)
+      return fail(FPSCAN_ERR_INVALID, "out partially overlaps %s", in->name);
+  FwdArgs a{gates, tokens, out, nullptr, nullptr, nullptr, rows, seqlen, dtype,
+            reverse ? 1 : 0, num_sms_current(), static_cast<cudaStream_t>(stream)};
+  return cuda_result(launch_fwd(a), "fpscan_scan_fwd launch");
+}
+
+int fpscan_scan_bwd(const void* gates, const void* y, const void* grad_out, void* dgates,
+                    void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                    void* stream) {
+  int64_t rows = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape(batch, dim, seqlen, kRefMinL, kRefMaxL, &rows));
+  if (rows == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(y, "y"));
+  FPSCAN_TRY(check_ptr(grad_out, "grad_out"));
+  FPSCAN_TRY(check_ptr(dgates, "dgates"));
+  FPSCAN_TRY(check_ptr(dtokens, "dtokens"));
+  const uintptr_t bytes = (uintptr_t)(rows * seqlen * dtype_size(dtype));
+  const Span in[3] = {{"gates", (uintptr_t)gates, (uintptr_t)gates + bytes},
+                      {"y", (uintptr_t)y, (uintptr_t)y + bytes},
+                      {"grad_out", (uintptr_t)grad_out, (uintptr_t)grad_out + bytes}};
+  const Span o[2] = {{"dgates", (uintptr_t)dgates, (uintptr_t)dgates + bytes},
+                     {"dtokens", (uintptr_t)dtokens, (uintptr_t)dtokens + bytes}};
+  if (overlaps(o[0], o[1])) return fail(FPSCAN_ERR_INVALID, "dgates overlaps dtokens");
+  for (const Span& os : o)
+    for (const Span& is : in)
+      if (overlaps(os, is)) return fail(FPSCAN_ERR_INVALID, "%s overlaps %s", os.name, is.name);
+  BwdArgs a{gates,   y,       grad_out, dgates, dtokens, nullptr, nullptr,
+            nullptr, rows,    seqlen,   dtype,  num_sms_current(),
+            static_cast<cudaStream_t>(stream)};
+  return cuda_result(launch_bwd(a), "fpscan_scan_bwd launch");
+}
+
+int fpscan_shard_fwd_reduce(const void* gates, const void* tokens, float* carry_a,
+                            float* carry_b, int64_t rows, int64_t seqlen, int dtype,
+                            void* stream) {
+  int64_t r = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape(rows, 1, seqlen, kRefMinL, kShardMaxL, &r));
+  if (r == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(tokens, "tokens"));
+  if (!carry_a || !carry_b) return fail(FPSCAN_ERR_INVALID, "carry_a/carry_b is NULL");
+  FwdArgs a{gates, tokens, nullptr, nullptr, carry_a, carry_b, r, seqlen, dtype, 0,
+            num_sms_current(), static_cast<cudaStream_t>(stream)};
+  return cuda_result(launch_fwd(a), "fpscan_shard_fwd_reduce launch");
+}
+
+int fpscan_shard_fwd_scan(const void* gates, const void* tokens, void* out, const float* y_init,
+                          int64_t rows, int64_t seqlen, int dtype, void* stream) {
+  int64_t r = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape(rows, 1, seqlen, kRefMinL, kShardMaxL, &r));
+  if (r == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(tokens, "tokens"));
+  FPSCAN_TRY(check_ptr(out, "out"));
+  if (!y_init) return fail(FPSCAN_ERR_INVALID, "y_init is NULL");
+  FwdArgs a{gates, tokens, out, y_init, nullptr, nullptr, r, seqlen, dtype, 0,
+            num_sms_current(), static_cast<cudaStream_t>(stream)};
+  return cuda_result(launch_fwd(a), "fpscan_shard_fwd_scan launch");
+}
+
+int fpscan_shard_bwd_reduce(const void* gates, const void* grad_out, float* carry_b,
+                            int64_t rows, int64_t seqlen, int dtype, void* stream) {
+  int64_t r = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape(rows, 1, seqlen, kRefMinL, kShardMaxL, &r));
+  if (r == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(grad_out, "grad_out"));
+  if (!carry_b) return fail(FPSCAN_ERR_INVALID, "carry_b is NULL");
+  BwdArgs a{gates,   nullptr, grad_out, nullptr, nullptr, nullptr, nullptr,
+            carry_b, r,       seqlen,   dtype,   num_sms_current(),
+            static_cast<cudaStream_t>(stream)};
+  return cuda_result(launch_bwd(a), "fpscan_shard_bwd_reduce launch");
+}
+
+int fpscan_shard_bwd_scan(const void* gates, const void* y, const void* grad_out, void* dgates,
+                          void* dtokens, const float* addend, const float* y_prev, int64_t rows,
+                          int64_t seqlen, int dtype, void* stream) {
+  int64_t r = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape(rows, 1, seqlen, kRefMinL, kShardMaxL, &r));
+  if (r == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(y, "y"));
+  FPSCAN_TRY(check_ptr(grad_out, "grad_out"));
+  FPSCAN_TRY(check_ptr(dgates, "dgates"));
+  FPSCAN_TRY(check_ptr(dtokens, "dtokens"));
+  if (!addend || !y_prev) return fail(FPSCAN_ERR_INVALID, "addend/y_prev is NULL");
+  BwdArgs a{gates,   y, grad_out, dgates, dtokens, addend, y_prev,
+            nullptr, r, seqlen,   dtype,  num_sms_current(),
+            static_cast<cudaStream_t>(stream)};
+  return cuda_result(launch_bwd(a), "fpscan_shard_bwd_scan launch");
+}
+
+int fpscan_carry_combine(const float* gathered, int world, int rank, int64_t rows, int reverse,
+                         float* out, void* stream) {
+  if (world < 1 || rank < 0 || rank >= world)
+    return fail(FPSCAN_ERR_INVALID, "invalid world (%d) / rank (%d)", world, rank);
+  if (rows < 0) return fail(FPSCAN_ERR_INVALID, "rows must be non-negative");
+  if (rows == 0) return ok();
+  if (!gathered || !out) return fail(FPSCAN_ERR_INVALID, "gathered/out is NULL");
+  return cuda_result(launch_carry_combine(gathered, world, rank, rows, reverse ? 1 : 0, out,
+                                          static_cast<cudaStream_t>(stream)),
+                     "fpscan_carry_combine launch");
+}
+
+int fpscan_device_status(unsigned* status, int clear) {
+  if (!status) return fail(FPSCAN_ERR_INVALID, "status is NULL");
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+  if (e != cudaSuccess) return cuda_result(e, "fpscan_device_status read");
+  if (clear && v) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
+    if (e != cudaSuccess) return cuda_result(e, "fpscan_device_status clear");
+  }
+  *status = v;
+  return ok();
+}
+
+}  // extern "C"

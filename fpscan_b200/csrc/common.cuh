@@ -1,0 +1,151 @@
+// Shared device helpers for the fpscan B200 kernels (sm_100a only).
+//
+// The scan operator is the first-order linear recurrence
+//     y[t] = g[t] * y[t-1] + x[t]
+// represented as affine maps (A, B): y -> A*y + B.  Composing an earlier map
+// (Ap, Bp) with a later one (A, B) gives (Ap*A, Bp*A + B); the scan of x over
+// g is the B component of the inclusive prefix composition.  All arithmetic
+// is fp32 regardless of the storage type, as in the reference kernel
+// (csrc/full_scan/full_scan.cu:87-111 accumulates in float).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+namespace fpscan {
+
+// Threads per CTA of every streaming kernel; one 16-byte vector per thread per
+// chunk, so a chunk is 4 KiB per tensor whatever the element type.
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kVecBytes = 16;
+constexpr int kChunkBytes = kThreads * kVecBytes;
+
+// Device-side status word.  Bounded waits that give up set a bit here instead
+// of hanging the GPU; the host reads and clears it through
+// fpscan_device_status().
+enum : unsigned { kStatusWaitTimeout = 1u };
+
+extern __device__ unsigned int g_status;
+
+// ---------------------------------------------------------------- conversion
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static constexpr int kVec = 4;
+  __device__ __forceinline__ static float load(float v) { return v; }
+  __device__ __forceinline__ static float store(float v) { return v; }
+};
+template <> struct Elem<__half> {
+  static constexpr int kVec = 8;
+  __device__ __forceinline__ static float load(__half v) { return __half2float(v); }
+  __device__ __forceinline__ static __half store(float v) { return __float2half_rn(v); }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int kVec = 8;
+  __device__ __forceinline__ static float load(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static __nv_bfloat16 store(float v) { return __float2bfloat16_rn(v); }
+};
+
+// One 16-byte vector viewed as kVec elements.
+template <typename T> union Vec16 {
+  uint4 raw;
+  T e[Elem<T>::kVec];
+};
+
+// ---------------------------------------------------------------- mbarrier / bulk copy
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Non-multicast 1-D bulk copy global -> shared, completing on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for phase `parity` of `bar`, giving up after ~2 s of wall time.  A bulk
+// copy from valid device memory always completes, so the limit only guards
+// against a fault elsewhere turning into a hung GPU.  Returns false on
+// timeout (and records it in g_status).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
+      atomicOr(&g_status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- scan combine
+// Inclusive Hillis-Steele scan of (A, B) pairs across `width` lanes
+// (width a power of two <= 32, segments aligned to multiples of width).
+__device__ __forceinline__ void warp_scan_pair(float& a, float& b, int lane, int width) {
+  const int seg_lane = lane & (width - 1);
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    if (d >= width) break;
+    const float pa = __shfl_up_sync(0xffffffffu, a, d);
+    const float pb = __shfl_up_sync(0xffffffffu, b, d);
+    if (seg_lane >= d) {
+      b = fmaf(pb, a, b);
+      a = pa * a;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- launch geometry
+// Rows are processed whole by one CTA ("tile" = consecutive rows).  When a row
+// is shorter than a chunk, a chunk holds several whole rows and the scan is
+// segmented at row boundaries, which fall on thread groups of L/kVec threads.
+struct TileGeom {
+  int64_t rows;           // batch*dim
+  int64_t seqlen;         // L
+  int64_t rows_per_tile;  // rows handled by one CTA
+  int64_t tiles;          // grid size
+};
+
+}  // namespace fpscan

@@ -1,0 +1,50 @@
+// Internal launcher interface between the C-ABI layer (capi.cu) and the
+// kernel translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace fpscan {
+
+enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+
+inline int dtype_size(int dt) { return dt == kF32 ? 4 : 2; }
+
+struct FwdArgs {
+  const void* gates;
+  const void* tokens;
+  void* out;            // nullptr: reduce only (carry-out required)
+  const float* init;    // nullptr: zero initial state (first gate ignored)
+  float* carry_a;       // nullptr: no carry-out; else per-row product of gates
+  float* carry_b;       //          and per-row final state
+  int64_t rows;
+  int64_t seqlen;
+  int dtype;
+  int reverse;
+  int num_sms;
+  cudaStream_t stream;
+};
+
+struct BwdArgs {
+  const void* gates;
+  const void* y;         // forward output; unused in reduce mode
+  const void* grad_out;
+  void* dgates;          // nullptr together with dtokens: reduce mode
+  void* dtokens;
+  const float* addend;   // nullptr: zero; else per-row value added at the row's last element
+  const float* y_prev;   // nullptr: zero; else per-row y just before the row's first element
+  float* carry_b;        // reduce mode: per-row gates[first] * dtokens[first]
+  int64_t rows;
+  int64_t seqlen;
+  int dtype;
+  int num_sms;
+  cudaStream_t stream;
+};
+
+cudaError_t launch_fwd(const FwdArgs& a);
+cudaError_t launch_bwd(const BwdArgs& a);
+cudaError_t launch_carry_combine(const float* gathered, int world, int rank, int64_t rows,
+                                 int reverse, float* out, cudaStream_t stream);
+
+}  // namespace fpscan

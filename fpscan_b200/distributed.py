@@ -1,0 +1,196 @@
+"""Multi-GPU scan: channel sharding and sequence sharding (one process per GPU).
+
+The reference has no multi-GPU path; these two modes extend its API.
+
+Channel sharding (``channel_slice`` / ``channel_sharded_pscan``): the
+batch*dim rows are independent, so each rank scans its contiguous block of
+rows with the single-GPU kernels and nothing is exchanged.
+
+Sequence sharding (``seq_sharded_pscan``): rank r holds positions
+[r*Lr, (r+1)*Lr) of every row.  A shard acts on its incoming state as an
+affine map y_out = A*y_in + B, so:
+
+forward
+  1. reduce: per row (A_r = prod gates, B_r = local scan's last value)
+     -- reads gates and tokens once, writes 2 floats per row;
+  2. all_gather_into_tensor of the [2, rows] fp32 maps (NCCL over NVLink);
+  3. combine maps of ranks < r into y_init (device kernel, no host sync);
+  4. scan with initial state y_init.
+backward (dtokens[t] = gates[t+1]*dtokens[t+1] + g[t], dgates[t] = dtokens[t]*y[t-1])
+  1. reduce: per row v_r = gates_r[0] * dtokens_r[0] with nothing entering
+     from the right; the map of shard r on the value entering it is
+     (A_r, v_r) with the same A_r as the forward (so no gate halo is needed);
+  2. all_gather of (A_r, v_r);
+  3. combine maps of ranks > r into the value entering at the last element;
+  4. fused backward with that addend and y_init (= y of the previous shard's
+     last element) for dgates at the first position.
+
+The device-side steps are behind ``LocalOps`` so the exchange logic can be
+exercised on CPU ranks (gloo) with a CPU implementation injected by tests;
+the default, ``CudaOps``, calls libfpscan_b200.so and is the only
+implementation in this package.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .ops import DTYPE_CODES, pscan, scan_backward, scan_forward, validate
+
+__all__ = [
+    "channel_slice",
+    "channel_sharded_pscan",
+    "seq_sharded_pscan",
+    "SeqShardedPScan",
+    "CudaOps",
+]
+
+
+# --------------------------------------------------------------------------- channel sharding
+def channel_slice(rows: int, rank: int, world: int) -> tuple[int, int]:
+    """[lo, hi) of the flattened batch*dim rows owned by ``rank``; the first
+    ``rows % world`` ranks get one extra row."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"invalid rank {rank} for world {world}")
+    base, extra = divmod(rows, world)
+    lo = rank * base + min(rank, extra)
+    hi = lo + base + (1 if rank < extra else 0)
+    return lo, hi
+
+
+def local_channels(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """This rank's rows of a (batch, dim, L) tensor, as a (1, rows_local, L) view."""
+    b, d, l = x.shape
+    lo, hi = channel_slice(b * d, rank, world)
+    return x.reshape(1, b * d, l)[:, lo:hi]
+
+
+def channel_sharded_pscan(gates_local: torch.Tensor, tokens_local: torch.Tensor) -> torch.Tensor:
+    """Differentiable scan of this rank's channel block: no communication."""
+    return pscan(gates_local, tokens_local)
+
+
+# --------------------------------------------------------------------------- sequence sharding
+class CudaOps:
+    """Device steps of the sequence-sharded scan, on libfpscan_b200.so."""
+
+    @staticmethod
+    def _rows_len(x: torch.Tensor):
+        return x.numel() // x.shape[-1], x.shape[-1]
+
+    @staticmethod
+    def _stream(x: torch.Tensor) -> int:
+        return torch.cuda.current_stream(x.device).cuda_stream
+
+    def fwd_reduce(self, gates, tokens):
+        rows, L = self._rows_len(tokens)
+        carry = torch.empty(2, rows, dtype=torch.float32, device=tokens.device)
+        _lib.call("fpscan_shard_fwd_reduce", gates.data_ptr(), tokens.data_ptr(),
+                  carry[0].data_ptr(), carry[1].data_ptr(), rows, L,
+                  DTYPE_CODES[tokens.dtype], self._stream(tokens))
+        return carry
+
+    def fwd_scan(self, gates, tokens, y_init):
+        rows, L = self._rows_len(tokens)
+        out = torch.empty_like(tokens)
+        _lib.call("fpscan_shard_fwd_scan", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
+                  y_init.data_ptr(), rows, L, DTYPE_CODES[tokens.dtype], self._stream(tokens))
+        return out
+
+    def fwd_scan_zero(self, gates, tokens):
+        return scan_forward(gates, tokens)
+
+    def bwd_reduce(self, gates, grad_out):
+        rows, L = self._rows_len(grad_out)
+        v = torch.empty(rows, dtype=torch.float32, device=grad_out.device)
+        _lib.call("fpscan_shard_bwd_reduce", gates.data_ptr(), grad_out.data_ptr(), v.data_ptr(),
+                  rows, L, DTYPE_CODES[grad_out.dtype], self._stream(grad_out))
+        return v
+
+    def bwd_scan(self, gates, y, grad_out, addend, y_prev):
+        rows, L = self._rows_len(grad_out)
+        dg = torch.empty_like(grad_out)
+        dt = torch.empty_like(grad_out)
+        _lib.call("fpscan_shard_bwd_scan", gates.data_ptr(), y.data_ptr(), grad_out.data_ptr(),
+                  dg.data_ptr(), dt.data_ptr(), addend.data_ptr(), y_prev.data_ptr(), rows, L,
+                  DTYPE_CODES[grad_out.dtype], self._stream(grad_out))
+        return dg, dt
+
+    def bwd_scan_zero(self, gates, y, grad_out):
+        return scan_backward(gates, y, grad_out)
+
+    def combine(self, gathered, world, rank, reverse):
+        rows = gathered.shape[-1]
+        out = torch.empty(rows, dtype=torch.float32, device=gathered.device)
+        _lib.call("fpscan_carry_combine", gathered.data_ptr(), world, rank, rows,
+                  1 if reverse else 0, out.data_ptr(), self._stream(gathered))
+        return out
+
+
+def _all_gather_maps(local: torch.Tensor, world: int, group) -> torch.Tensor:
+    """[2, rows] fp32 per rank -> [world, 2, rows]."""
+    flat = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                       device=local.device)
+    dist.all_gather_into_tensor(flat, local.contiguous(), group=group)
+    return flat.view((world,) + tuple(local.shape))
+
+
+def _validate_local(gates: torch.Tensor, tokens: torch.Tensor, on_cuda: bool) -> None:
+    if on_cuda:
+        validate(gates, tokens)
+    else:
+        if gates.shape != tokens.shape or gates.dtype != tokens.dtype:
+            raise RuntimeError("gates and tokens must have the same shape and dtype")
+    L = tokens.shape[-1]
+    if L < 32 or L & (L - 1):
+        raise RuntimeError(f"local seqlen must be a power of 2 >= 32 (got {L})")
+
+
+class SeqShardedPScan(torch.autograd.Function):
+    """Differentiable scan over sequences split along seqlen across ranks."""
+
+    @staticmethod
+    def forward(ctx, gates, tokens, group, ops):
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        carry = ops.fwd_reduce(gates, tokens)                    # [2, rows]: (A_r, B_r)
+        gathered = _all_gather_maps(carry, world, group)         # [world, 2, rows]
+        y_init = ops.combine(gathered, world, rank, reverse=False)
+        if rank == 0:
+            y = ops.fwd_scan_zero(gates, tokens)
+        else:
+            y = ops.fwd_scan(gates, tokens, y_init)
+        ctx.save_for_backward(gates, y, carry[0].clone(), y_init)
+        ctx.group, ctx.ops, ctx.world, ctx.rank = group, ops, world, rank
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        gates, y, a_local, y_init = ctx.saved_tensors
+        ops, world, rank = ctx.ops, ctx.world, ctx.rank
+        grad_out = grad_out.contiguous()
+        v = ops.bwd_reduce(gates, grad_out)
+        gathered = _all_gather_maps(torch.stack([a_local, v]), world, ctx.group)
+        addend = ops.combine(gathered, world, rank, reverse=True)
+        if world == 1:
+            dg, dt = ops.bwd_scan_zero(gates, y, grad_out)
+        else:
+            dg, dt = ops.bwd_scan(gates, y, grad_out, addend, y_init)
+        return dg, dt, None, None
+
+
+def seq_sharded_pscan(gates_local: torch.Tensor, tokens_local: torch.Tensor,
+                      group: Optional[dist.ProcessGroup] = None, ops=None) -> torch.Tensor:
+    """Differentiable scan of this rank's sequence shard ``(batch, dim, L/world)``.
+
+    Rank r must hold positions [r*L/world, (r+1)*L/world) of every row, all
+    ranks the same rows.  Collectives: one all-gather of 2*rows fp32 forward
+    and one backward.
+    """
+    if ops is None:
+        ops = CudaOps()
+    _validate_local(gates_local, tokens_local, isinstance(ops, CudaOps))
+    return SeqShardedPScan.apply(gates_local, tokens_local, group, ops)

@@ -1,0 +1,140 @@
+"""Drop-in mirror of the reference's Python op layer (fpscan/ops.py).
+
+Same public names, signatures and error type as the reference:
+
+* ``scan_forward(gates, tokens, reverse=False, out=None)`` -- fpscan/ops.py:47-58
+* ``PScan`` autograd function                              -- fpscan/ops.py:61-83
+* ``pscan(gates, tokens)``                                 -- fpscan/ops.py:86-87
+
+Tensors are ``(batch, dim, seqlen)``, contiguous, CUDA, float32 / float16 /
+bfloat16, power-of-two seqlen in [32, 65536]; the scan runs along the last
+axis with a zero initial state.  Invalid input raises ``RuntimeError`` as the
+reference's TORCH_CHECKs do (csrc/full_scan/full_scan.h:7-15,
+csrc/full_scan/full_scan.cu:181-182, 232, 240-256).  The work is done by
+``libfpscan_b200.so`` on the caller's current CUDA stream; there is no CPU
+path.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+__all__ = ["pscan", "scan_forward", "PScan"]
+
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+MIN_SEQLEN = 32
+MAX_SEQLEN = 65536
+
+
+def _check_input(x: torch.Tensor, name: str) -> None:
+    # Order and wording follow CHECK_INPUT (csrc/full_scan/full_scan.h:7-15).
+    if not isinstance(x, torch.Tensor):
+        raise RuntimeError(f"{name} must be a torch.Tensor")
+    if not x.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if not x.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if x.dtype not in DTYPE_CODES:
+        raise RuntimeError(f"{name} must be float16 or bfloat16 or float32")
+
+
+def validate(gates: torch.Tensor, tokens: torch.Tensor,
+             out: Optional[torch.Tensor] = None) -> None:
+    """Raise RuntimeError unless (gates, tokens[, out]) form a valid scan call."""
+    _check_input(gates, "gates")
+    _check_input(tokens, "tokens")
+    validate_layout(gates, tokens, out)
+
+
+def validate_layout(gates: torch.Tensor, tokens: torch.Tensor,
+                    out: Optional[torch.Tensor] = None) -> None:
+    """Device-independent checks (shape, dtype, seqlen, out); CPU-testable."""
+    if tokens.dim() != 3:
+        raise RuntimeError(f"tokens must be 3-D (batch, dim, seqlen), got {tuple(tokens.shape)}")
+    if gates.shape != tokens.shape:
+        raise RuntimeError(
+            f"gates {tuple(gates.shape)} and tokens {tuple(tokens.shape)} must have the same shape")
+    if gates.dtype != tokens.dtype:
+        raise RuntimeError(f"gates dtype {gates.dtype} must equal tokens dtype {tokens.dtype}")
+    if gates.device != tokens.device:
+        raise RuntimeError("gates and tokens must be on the same device")
+    seqlen = tokens.shape[-1]
+    if seqlen & (seqlen - 1) or not MIN_SEQLEN <= seqlen <= MAX_SEQLEN:
+        raise RuntimeError(
+            f"seqlen must be a power of 2, >= {MIN_SEQLEN}, <= {MAX_SEQLEN} (got {seqlen})")
+    if out is not None:
+        if out.shape != tokens.shape or out.dtype != tokens.dtype or out.device != tokens.device:
+            raise RuntimeError("out must match tokens in shape, dtype and device")
+        if not out.is_contiguous():
+            raise RuntimeError("out must be contiguous")
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def fullscan_forward(gates: torch.Tensor, tokens: torch.Tensor, out: torch.Tensor,
+                     reverse: bool) -> torch.Tensor:
+    """Same contract as the reference extension's ``fullscan_forward``
+    (csrc/main.cpp:10 -> warpscan_fwd): validates, scans into ``out``, returns it."""
+    validate(gates, tokens, out)
+    b, d, l = tokens.shape
+    with torch.cuda.device(tokens.device):
+        _lib.call("fpscan_scan_fwd", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
+                  b, d, l, DTYPE_CODES[tokens.dtype], 1 if reverse else 0,
+                  _stream_ptr(tokens.device))
+    return out
+
+
+def scan_forward(gates: torch.Tensor, tokens: torch.Tensor, reverse: bool = False,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Linear-recurrence scan y[t] = gates[t]*y[t-1] + tokens[t] (no autograd).
+
+    ``reverse=True`` scans from the end: y[t] = gates[t]*y[t+1] + tokens[t].
+    ``out`` (optional) receives the result and is returned.
+    """
+    _lib.load()  # fail loudly before allocating if the library is missing
+    if out is None:
+        out = torch.empty_like(tokens)
+    return fullscan_forward(gates, tokens, out, reverse)
+
+
+def scan_backward(gates: torch.Tensor, y: torch.Tensor, grad_output: torch.Tensor):
+    """Fused gradient of ``y = scan_forward(gates, tokens)``: one launch
+    returning ``(grad_gates, grad_tokens)``.  Equals the reference's
+    PScan.backward composition (fpscan/ops.py:70-83)."""
+    validate(gates, grad_output)
+    validate(gates, y)
+    dgates = torch.empty_like(grad_output)
+    dtokens = torch.empty_like(grad_output)
+    b, d, l = grad_output.shape
+    with torch.cuda.device(grad_output.device):
+        _lib.call("fpscan_scan_bwd", gates.data_ptr(), y.data_ptr(), grad_output.data_ptr(),
+                  dgates.data_ptr(), dtokens.data_ptr(), b, d, l,
+                  DTYPE_CODES[grad_output.dtype], _stream_ptr(grad_output.device))
+    return dgates, dtokens
+
+
+class PScan(torch.autograd.Function):
+    """Differentiable scan; saves (gates, out) like fpscan/ops.py:64-67 and
+    computes both gradients in one fused kernel."""
+
+    @staticmethod
+    def forward(ctx, gates: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
+        out = scan_forward(gates, tokens)
+        ctx.save_for_backward(gates, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output: torch.Tensor):
+        gates, out = ctx.saved_tensors
+        grad_output = grad_output.contiguous()
+        return scan_backward(gates, out, grad_output)
+
+
+def pscan(gates: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
+    """Differentiable scan (fpscan/ops.py:86-87)."""
+    return PScan.apply(gates, tokens)

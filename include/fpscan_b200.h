@@ -1,0 +1,119 @@
+/*
+ * fpscan_b200 — C ABI of the B200 (sm_100a) linear-recurrence scan library.
+ *
+ *     y[t] = gates[t] * y[t-1] + tokens[t],   y[-1] = 0,
+ * along the last axis of contiguous (batch, dim, seqlen) tensors.
+ *
+ * Conventions for every entry point:
+ *   - All pointers are device pointers of the CURRENT CUDA device, 16-byte
+ *     aligned; tensors are row-major (rows = batch*dim rows of `seqlen`
+ *     elements).  Element type is given by `dtype` (FPSCAN_F32/F16/BF16);
+ *     per-row carry buffers are always fp32.
+ *   - Work is enqueued asynchronously on `stream` (a cudaStream_t; NULL is
+ *     the legacy default stream).  The library never allocates device
+ *     memory and keeps no per-call state; calls are re-entrant.
+ *   - Return 0 on success.  Non-zero: FPSCAN_ERR_INVALID (bad argument,
+ *     nothing launched) or FPSCAN_ERR_CUDA (launch failed); the message is in
+ *     fpscan_last_error() of the calling thread.
+ *   - Arithmetic is fp32 for every storage type.
+ */
+#ifndef FPSCAN_B200_H
+#define FPSCAN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FPSCAN_OK 0
+#define FPSCAN_ERR_INVALID 1
+#define FPSCAN_ERR_CUDA 2
+
+#define FPSCAN_F32 0
+#define FPSCAN_F16 1
+#define FPSCAN_BF16 2
+
+#define FPSCAN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FPSCAN_API __attribute__((visibility("default")))
+#else
+#define FPSCAN_API
+#endif
+
+/* Version of this ABI (FPSCAN_ABI_VERSION). */
+FPSCAN_API int fpscan_abi_version(void);
+
+/*
+ * Forward or reverse scan, zero initial state; the gate of the first element
+ * in scan order is ignored.  `out` may be exactly `tokens` or `gates`
+ * (in place); any other overlap is rejected.  seqlen: power of two in
+ * [32, 65536].
+ * Replaces fpscan._C.fullscan_forward(gates, tokens, out, reverse)
+ * (reference csrc/main.cpp:10 -> warpscan_fwd, csrc/full_scan/full_scan.h:26-36,
+ * warpscan_forward, csrc/full_scan/full_scan.cu:238-258).
+ */
+FPSCAN_API int fpscan_scan_fwd(const void* gates, const void* tokens, void* out, int64_t batch,
+                    int64_t dim, int64_t seqlen, int dtype, int reverse, void* stream);
+
+/*
+ * Fused backward of y = scan(gates, tokens):
+ *   dtokens[t] = gates[t+1]*dtokens[t+1] + grad_out[t]  (last element: grad_out)
+ *   dgates[t]  = dtokens[t] * y[t-1]                      (first element: 0*dtokens)
+ * One launch, reads gates/y/grad_out once, writes dgates/dtokens.  Outputs
+ * must not overlap any input or each other.  seqlen as fpscan_scan_fwd.
+ * Replaces the composition in PScan.backward (reference fpscan/ops.py:70-83:
+ * two torch.cat shifts, a reverse fullscan_forward and a multiply).
+ */
+FPSCAN_API int fpscan_scan_bwd(const void* gates, const void* y, const void* grad_out, void* dgates,
+                    void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                    void* stream);
+
+/* ---- Sequence-sharded building blocks (no reference counterpart: the
+ * reference has no multi-GPU path).  A shard holds `rows` rows of `seqlen`
+ * (power of two, >= 32, <= 2^24) consecutive positions of longer sequences. */
+
+/* Per row: carry_a = product of all gates, carry_b = scan's last value with
+ * zero initial state.  Reads gates and tokens, writes 2 floats per row. */
+FPSCAN_API int fpscan_shard_fwd_reduce(const void* gates, const void* tokens, float* carry_a,
+                            float* carry_b, int64_t rows, int64_t seqlen, int dtype,
+                            void* stream);
+
+/* Forward scan with per-row initial state y_init (y[0] = gates[0]*y_init + tokens[0]). */
+FPSCAN_API int fpscan_shard_fwd_scan(const void* gates, const void* tokens, void* out,
+                          const float* y_init, int64_t rows, int64_t seqlen, int dtype,
+                          void* stream);
+
+/* Per row: carry_b = gates[0] * dtokens[0], dtokens computed with zero value
+ * entering from the right.  Reads gates and grad_out. */
+FPSCAN_API int fpscan_shard_bwd_reduce(const void* gates, const void* grad_out, float* carry_b,
+                            int64_t rows, int64_t seqlen, int dtype, void* stream);
+
+/* Fused backward of a shard: `addend` (per row) enters at the last element
+ * (dtokens[L-1] = addend + grad_out[L-1]); `y_prev` (per row) is y just
+ * before the shard's first element, used for dgates[0]. */
+FPSCAN_API int fpscan_shard_bwd_scan(const void* gates, const void* y, const void* grad_out,
+                          void* dgates, void* dtokens, const float* addend,
+                          const float* y_prev, int64_t rows, int64_t seqlen, int dtype,
+                          void* stream);
+
+/* Fold gathered per-shard maps.  `gathered` is fp32 [world][2][rows]
+ * (A then B).  reverse=0: out = compose shards 0..rank-1 applied to 0;
+ * reverse=1: compose shards world-1..rank+1.  out: fp32 [rows]. */
+FPSCAN_API int fpscan_carry_combine(const float* gathered, int world, int rank, int64_t rows,
+                         int reverse, float* out, void* stream);
+
+/* Message of the last failed call on this thread ("" if none). */
+FPSCAN_API const char* fpscan_last_error(void);
+
+/* Synchronously read (and if `clear`, reset) the current device's status
+ * word.  Bit 0: a kernel gave up a bounded wait (results of that launch are
+ * not valid).  0 = healthy. */
+FPSCAN_API int fpscan_device_status(unsigned* status, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FPSCAN_B200_H */

@@ -1,0 +1,125 @@
+"""Host-side logic that needs no GPU: the C ABI loads and exports every
+declared symbol, argument validation (C and Python) mirrors the reference's
+errors, channel partitioning."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+import torch
+
+import fpscan_b200
+from fpscan_b200 import _lib, ops
+from fpscan_b200.distributed import channel_slice
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    names = []
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        names += re.findall(r"FPSCAN_API\s+[\w\s\*]+?\b(fpscan_\w+)\s*\(", open(h).read())
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    names = _declared_symbols()
+    assert "fpscan_scan_fwd" in names and "fpscan_scan_bwd" in names
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
+
+
+def test_abi_version():
+    assert _lib.load().fpscan_abi_version() == _lib.EXPECTED_ABI_VERSION
+
+
+def _fwd(gates=16, tokens=16, out=16, b=1, d=1, l=32, dtype=0, rev=0):
+    lib = _lib.load()
+    return lib.fpscan_scan_fwd(gates, tokens, out, b, d, l, dtype, rev, None)
+
+
+@pytest.mark.parametrize("l", [0, 16, 30, 48, 131072])
+def test_c_abi_rejects_bad_seqlen(l):
+    # csrc/full_scan/full_scan.cu:232: seqlen must be a power of 2 in [32, 65536]
+    assert _fwd(l=l) == 1
+    assert b"seqlen" in _lib.load().fpscan_last_error()
+
+
+def test_c_abi_rejects_bad_dtype_null_and_misaligned():
+    lib = _lib.load()
+    assert _fwd(dtype=7) == 1 and b"dtype" in lib.fpscan_last_error()
+    assert _fwd(gates=0) == 1 and b"NULL" in lib.fpscan_last_error()
+    assert _fwd(tokens=24) == 1 and b"aligned" in lib.fpscan_last_error()
+    assert _fwd(b=-1) == 1
+
+
+def test_c_abi_rejects_partial_overlap():
+    lib = _lib.load()
+    assert _fwd(gates=4096, tokens=8192, out=8192 + 64, l=32) == 1
+    assert b"overlap" in lib.fpscan_last_error()
+    rc = lib.fpscan_scan_bwd(4096, 1 << 20, 2 << 20, 4096 + 16, 3 << 20, 1, 1, 32, 0, None)
+    assert rc == 1 and b"overlap" in lib.fpscan_last_error()
+
+
+def test_c_abi_empty_is_noop():
+    # batch*dim == 0 launches nothing and succeeds (even without a GPU).
+    assert _fwd(b=0) == 0
+    assert _lib.load().fpscan_scan_bwd(0, 0, 0, 0, 0, 0, 4, 64, 0, None) == 0
+
+
+def test_carry_combine_arg_checks():
+    lib = _lib.load()
+    assert lib.fpscan_carry_combine(16, 2, 2, 8, 0, 32, None) == 1
+    assert lib.fpscan_carry_combine(16, 0, 0, 8, 0, 32, None) == 1
+
+
+def test_python_rejects_cpu_tensors_like_reference():
+    g = torch.rand(1, 1, 32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fpscan_b200.scan_forward(g, g)
+
+
+@pytest.mark.parametrize("case", ["pow2", "range", "shape", "dtype", "ndim", "out"])
+def test_layout_validation(case):
+    g = torch.rand(2, 3, 64)
+    x = torch.rand(2, 3, 64)
+    out = None
+    if case == "pow2":
+        g, x = g[..., :30].contiguous(), x[..., :30].contiguous()
+    elif case == "range":
+        g, x = torch.rand(1, 1, 16), torch.rand(1, 1, 16)
+    elif case == "shape":
+        x = torch.rand(2, 4, 64)
+    elif case == "dtype":
+        x = x.half()
+    elif case == "ndim":
+        g, x = g[0], x[0]
+    elif case == "out":
+        out = torch.empty(2, 3, 32)
+    with pytest.raises(RuntimeError):
+        ops.validate_layout(g, x, out)
+
+
+def test_layout_validation_accepts_reference_shapes():
+    for l in [32, 64, 4096, 65536]:
+        t = torch.empty(1, 1, l)
+        ops.validate_layout(t, t, torch.empty_like(t))
+
+
+@pytest.mark.parametrize("rows,world", [(512, 1), (512, 8), (81920, 8), (7, 3), (3, 8)])
+def test_channel_slice_partitions_rows(rows, world):
+    spans = [channel_slice(rows, r, world) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == rows
+    for (a, b), (c, d) in zip(spans, spans[1:]):
+        assert b == c
+    sizes = [b - a for a, b in spans]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def test_reference_style_extension_shim():
+    from fpscan_b200 import _C
+
+    assert hasattr(_C, "fullscan_forward")

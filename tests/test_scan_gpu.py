@@ -1,0 +1,370 @@
+"""GPU parity tests: fpscan_b200 (through its C ABI) against the CPU oracle,
+the golden vectors made by the reference's own code, the reference's own CUDA
+kernel (built from its sources into oracle/_ref) and size-independent
+properties at the BASELINE configurations.
+
+The first block mirrors the reference's tests/test_fpscan.py case for case
+(same names, inputs, seeds and tolerances).  On top of the reference's
+assert_close tolerances every comparison with the float64 oracle also checks
+the normwise bound max|got-ref|/max|ref| <= 1e-5 (fp32) / 1e-2 (fp16, bf16).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import fpscan_b200 as fpscan
+import oracle
+from fpscan_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+DEVICE = "cuda"
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+ALL_SEQLENS = [32, 64, 128, 256, 512, 1024, 2048, 4096, 8192, 16384, 32768, 65536]
+HALF_SEQLENS = [32, 64, 128, 256, 512, 1024, 2048, 4096]
+DTYPES = [torch.float32, torch.float16, torch.bfloat16]
+
+# reference tests/test_fpscan.py:18-22
+TOL = {
+    torch.float32: dict(atol=2e-3, rtol=2e-3),
+    torch.float16: dict(atol=3e-2, rtol=3e-2),
+    torch.bfloat16: dict(atol=6e-2, rtol=6e-2),
+}
+# north-star normwise tolerance vs float64
+NORM_TOL = {torch.float32: 1e-5, torch.float16: 1e-2, torch.bfloat16: 1e-2}
+
+
+def _make_inputs(batch, dim, seqlen, dtype, seed=0):
+    # reference tests/test_fpscan.py:25-29
+    gen = torch.Generator(device=DEVICE).manual_seed(seed)
+    gates = 0.99 + 0.01 * torch.rand(batch, dim, seqlen, generator=gen, device=DEVICE)
+    tokens = torch.randn(batch, dim, seqlen, generator=gen, device=DEVICE) / seqlen
+    return gates.to(dtype).contiguous(), tokens.to(dtype).contiguous()
+
+
+def _np64(t):
+    return t.detach().double().cpu().numpy()
+
+
+def _check(got, ref, dtype, what=""):
+    ref_t = torch.from_numpy(np.asarray(ref, dtype=np.float64))
+    got_t = got.detach().double().cpu()
+    torch.testing.assert_close(got_t, ref_t, **TOL[dtype])
+    err = oracle.normwise_error(got_t.numpy(), ref_t.numpy())
+    assert err <= NORM_TOL[dtype], f"{what} normwise error {err:.3e} > {NORM_TOL[dtype]}"
+
+
+def _dtype_seqlens():
+    for seqlen in ALL_SEQLENS:
+        yield torch.float32, seqlen
+    for seqlen in HALF_SEQLENS:
+        yield torch.float16, seqlen
+        yield torch.bfloat16, seqlen
+
+
+# ----------------------------------------------------------------- reference test mirror
+@pytest.mark.parametrize("dtype,seqlen", list(_dtype_seqlens()))
+def test_forward_matches_oracle(dtype, seqlen):
+    gates, tokens = _make_inputs(2, 4, seqlen, dtype, seed=seqlen)
+    out = fpscan.scan_forward(gates, tokens)
+    assert out.shape == tokens.shape
+    assert out.dtype == dtype
+    _check(out, oracle.scan_f64(_np64(gates), _np64(tokens)), dtype, "forward")
+
+
+@pytest.mark.parametrize("seqlen", ALL_SEQLENS)
+def test_reverse_matches_oracle(seqlen):
+    gates, tokens = _make_inputs(2, 4, seqlen, torch.float32, seed=seqlen + 1)
+    out = fpscan.scan_forward(gates, tokens, reverse=True)
+    _check(out, oracle.scan_f64(_np64(gates), _np64(tokens), reverse=True), torch.float32)
+
+
+@pytest.mark.parametrize("seqlen", [32, 256, 1024, 4096])
+def test_agrees_with_torch_parallel_baseline(seqlen):
+    gates, tokens = _make_inputs(2, 4, seqlen, torch.float32, seed=seqlen + 2)
+    out = fpscan.scan_forward(gates, tokens)
+    baseline = oracle.parallel_scan_torch(gates.double(), tokens.double())
+    _check(out, baseline.cpu().numpy(), torch.float32)
+
+
+@pytest.mark.parametrize("seqlen", [32, 128, 512, 2048, 8192])
+def test_backward_matches_oracle(seqlen):
+    gates, tokens = _make_inputs(2, 4, seqlen, torch.float32, seed=seqlen + 3)
+    g = gates.clone().requires_grad_()
+    x = tokens.clone().requires_grad_()
+    grad_seed = torch.Generator(device=DEVICE).manual_seed(seqlen + 4)
+    weight = torch.randn(*tokens.shape, generator=grad_seed, device=DEVICE)
+    out = fpscan.pscan(g, x)
+    (out * weight).sum().backward()
+    y64 = oracle.scan_f64(_np64(gates), _np64(tokens))
+    dg, dt = oracle.scan_bwd_f64(_np64(gates), y64, _np64(weight))
+    _check(g.grad, dg, torch.float32, "dgates")
+    _check(x.grad, dt, torch.float32, "dtokens")
+
+
+def test_non_power_of_two_seqlen_raises():
+    gates, tokens = _make_inputs(1, 1, 32, torch.float32)
+    with pytest.raises(RuntimeError):
+        fpscan.scan_forward(gates[..., :30].contiguous(), tokens[..., :30].contiguous())
+
+
+def test_non_contiguous_raises():
+    gates, tokens = _make_inputs(2, 4, 64, torch.float32)
+    with pytest.raises(RuntimeError):
+        fpscan.scan_forward(gates.transpose(1, 2), tokens.transpose(1, 2))
+
+
+# ----------------------------------------------------------------- beyond the reference's tests
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("seqlen", [32, 512, 8192, 65536])
+def test_reverse_half(dtype, seqlen):
+    gates, tokens = _make_inputs(2, 3, seqlen, dtype, seed=seqlen + 9)
+    out = fpscan.scan_forward(gates, tokens, reverse=True)
+    _check(out, oracle.scan_f64(_np64(gates), _np64(tokens), reverse=True), dtype, "reverse")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("seqlen", [32, 64, 256, 1024, 2048, 4096, 16384, 65536])
+def test_backward_all_dtypes(dtype, seqlen):
+    gates, tokens = _make_inputs(3, 5, seqlen, dtype, seed=seqlen + 13)
+    gen = torch.Generator(device=DEVICE).manual_seed(seqlen)
+    go = torch.randn(3, 5, seqlen, generator=gen, device=DEVICE).to(dtype)
+    g = gates.clone().requires_grad_()
+    x = tokens.clone().requires_grad_()
+    y = fpscan.pscan(g, x)
+    dg_t, dt_t = torch.autograd.grad(y, (g, x), go)
+    y64 = oracle.scan_f64(_np64(gates), _np64(tokens))
+    _check(y, y64, dtype, "y")
+    dg, dt = oracle.scan_bwd_f64(_np64(gates), y64, _np64(go))
+    _check(dt_t, dt, dtype, "dtokens")
+    _check(dg_t, dg, dtype, "dgates")
+
+
+@pytest.mark.parametrize("batch,dim", [(1, 1), (1, 3), (3, 5), (2, 37), (5, 300)])
+@pytest.mark.parametrize("seqlen", [32, 128, 1024, 4096])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_ragged_row_counts(batch, dim, seqlen, dtype):
+    # row counts that leave partial tiles / partial chunks
+    gates, tokens = _make_inputs(batch, dim, seqlen, dtype, seed=batch * 1000 + dim)
+    for rev in (False, True):
+        out = fpscan.scan_forward(gates, tokens, reverse=rev)
+        _check(out, oracle.scan_f64(_np64(gates), _np64(tokens), reverse=rev), dtype)
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in json.load(
+    open(os.path.join(HERE, "golden", "golden_meta.json")))["cases"]])
+def test_golden_vectors(name):
+    gold = np.load(os.path.join(HERE, "golden", "golden.npz"))
+    dtype = getattr(torch, name.split("_")[1])
+    g = torch.from_numpy(gold[f"{name}/gates"]).to(DEVICE, dtype)
+    x = torch.from_numpy(gold[f"{name}/tokens"]).to(DEVICE, dtype)
+    _check(fpscan.scan_forward(g, x), gold[f"{name}/y"], dtype, name)
+    if f"{name}/y_rev" in gold.files:
+        _check(fpscan.scan_forward(g, x, reverse=True), gold[f"{name}/y_rev"], dtype, name)
+    if f"{name}/dgates" in gold.files:
+        go = torch.from_numpy(gold[f"{name}/grad_out"]).to(DEVICE, dtype)
+        gg, xx = g.clone().requires_grad_(), x.clone().requires_grad_()
+        dg, dt = torch.autograd.grad(fpscan.pscan(gg, xx), (gg, xx), go)
+        _check(dt, gold[f"{name}/dtokens"], dtype, name + " dtokens")
+        _check(dg, gold[f"{name}/dgates"], dtype, name + " dgates")
+
+
+def test_out_argument_and_in_place():
+    gates, tokens = _make_inputs(2, 4, 1024, torch.float32, seed=3)
+    ref = oracle.scan_f64(_np64(gates), _np64(tokens))
+    out = torch.empty_like(tokens)
+    assert fpscan.scan_forward(gates, tokens, out=out) is out
+    _check(out, ref, torch.float32)
+    t2 = tokens.clone()
+    fpscan.scan_forward(gates, t2, out=t2)  # in place over tokens
+    _check(t2, ref, torch.float32)
+
+
+def test_empty_batch():
+    g = torch.empty(0, 4, 64, device=DEVICE)
+    assert fpscan.scan_forward(g, g).shape == (0, 4, 64)
+
+
+def test_first_gate_is_ignored_like_reference():
+    # reference kernel forces the first gate to 1 (csrc/full_scan/full_scan.cu:96)
+    gates, tokens = _make_inputs(2, 3, 4096, torch.float32, seed=1)
+    gates[..., 0] = float("inf")
+    out = fpscan.scan_forward(gates, tokens)
+    g = _np64(gates)
+    g[..., 0] = 0.0
+    _check(out, oracle.scan_f64(g, _np64(tokens)), torch.float32)
+    gates[..., -1] = float("nan")
+    out = fpscan.scan_forward(gates, tokens, reverse=True)
+    g = _np64(gates)
+    g[..., -1] = 0.0
+    _check(out, oracle.scan_f64(g, _np64(tokens), reverse=True), torch.float32)
+
+
+def test_mismatched_dtype_raises():
+    gates, tokens = _make_inputs(1, 2, 64, torch.float32)
+    with pytest.raises(RuntimeError):
+        fpscan.scan_forward(gates.half(), tokens)
+
+
+def test_reference_extension_shim_contract():
+    from fpscan_b200 import _C
+
+    gates, tokens = _make_inputs(2, 4, 256, torch.float32, seed=4)
+    out = torch.empty_like(tokens)
+    ret = _C.fullscan_forward(gates, tokens, out, True)
+    assert ret is out
+    _check(out, oracle.scan_f64(_np64(gates), _np64(tokens), reverse=True), torch.float32)
+
+
+# ----------------------------------------------------------------- vs the reference's kernel
+_REF = oracle.load_reference_kernel()
+
+
+@pytest.mark.skipif(_REF is None, reason="reference kernel not built (oracle/build_ref.py)")
+@pytest.mark.parametrize("dtype,seqlen", [(torch.float32, L) for L in ALL_SEQLENS]
+                         + [(torch.bfloat16, L) for L in (32, 1024, 8192)]
+                         + [(torch.float16, L) for L in (64, 4096)])
+def test_agrees_with_reference_kernel(dtype, seqlen):
+    gates, tokens = _make_inputs(2, 8, seqlen, dtype, seed=seqlen + 21)
+    for rev in (False, True):
+        ref = torch.empty_like(tokens)
+        _REF.fullscan_forward(gates, tokens, ref, rev)
+        out = fpscan.scan_forward(gates, tokens, reverse=rev)
+        torch.testing.assert_close(out.double(), ref.double(), **TOL[dtype])
+        assert oracle.normwise_error(_np64(out), _np64(ref)) <= NORM_TOL[dtype]
+
+
+@pytest.mark.skipif(_REF is None, reason="reference kernel not built (oracle/build_ref.py)")
+def test_backward_agrees_with_reference_composition():
+    gates, tokens = _make_inputs(4, 64, 8192, torch.bfloat16, seed=77)
+    gen = torch.Generator(device=DEVICE).manual_seed(78)
+    go = torch.randn(4, 64, 8192, generator=gen, device=DEVICE).to(torch.bfloat16)
+
+    def ref_scan(g, x, rev):
+        o = torch.empty_like(x)
+        _REF.fullscan_forward(g, x, o, rev)
+        return o
+
+    y_ref = ref_scan(gates, tokens, False)
+    dg_ref, dt_ref = oracle.pscan_backward_formula(gates, y_ref, go, ref_scan)
+    y = fpscan.scan_forward(gates, tokens)
+    dg, dt = fpscan.scan_backward(gates, y, go)
+    for a, b in ((y, y_ref), (dt, dt_ref), (dg, dg_ref)):
+        assert oracle.normwise_error(_np64(a), _np64(b)) <= 1e-2
+
+
+# ----------------------------------------------------------------- BASELINE configs, full size
+def _sample_rows_check(gates, tokens, y, go=None, dg=None, dt=None, n=48, tol=1e-2, seed=0):
+    """Compare n random rows of a full-size run with the float64 oracle."""
+    L = tokens.shape[-1]
+    rows = tokens.numel() // L
+    idx = torch.randperm(rows, generator=torch.Generator().manual_seed(seed))[:n].to(DEVICE)
+
+    def pick(t):
+        return _np64(t.reshape(rows, L).index_select(0, idx))
+
+    g64, x64 = pick(gates), pick(tokens)
+    y64 = oracle.scan_f64(g64, x64)
+    assert oracle.normwise_error(pick(y), y64) <= tol
+    if go is not None:
+        dg64, dt64 = oracle.scan_bwd_f64(g64, y64, pick(go))
+        assert oracle.normwise_error(pick(dt), dt64) <= tol
+        assert oracle.normwise_error(pick(dg), dg64) <= tol
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_config3_mamba_like_fwd_bwd(dtype):
+    # batch 8, dim 2048, seqlen 8192, gates = sigmoid(N(2,1))
+    gen = torch.Generator(device=DEVICE).manual_seed(3)
+    shape = (8, 2048, 8192)
+    gates = torch.sigmoid(torch.randn(shape, generator=gen, device=DEVICE) + 2).to(dtype)
+    tokens = (torch.randn(shape, generator=gen, device=DEVICE) * 0.1).to(dtype)
+    go = torch.randn(shape, generator=gen, device=DEVICE).to(dtype)
+    y = fpscan.scan_forward(gates, tokens)
+    dg, dt = fpscan.scan_backward(gates, y, go)
+    _sample_rows_check(gates, tokens, y, go, dg, dt)
+
+
+def test_config4_full_size_bf16():
+    # BASELINE config 4 (single GPU, all channels): 16 x 5120 x 16384 bf16
+    gen = torch.Generator(device=DEVICE).manual_seed(4)
+    shape = (16, 5120, 16384)
+    z = torch.randn(shape, generator=gen, device=DEVICE) - 1
+    gates = torch.exp(-torch.nn.functional.softplus(z)).to(torch.bfloat16)
+    del z
+    tokens = torch.randn(shape, generator=gen, device=DEVICE).to(torch.bfloat16)
+    go = torch.randn(shape, generator=gen, device=DEVICE).to(torch.bfloat16)
+    y = fpscan.scan_forward(gates, tokens)
+    dg, dt = fpscan.scan_backward(gates, y, go)
+    _sample_rows_check(gates, tokens, y, go, dg, dt, seed=4)
+    # linearity of the scan in tokens (size-independent property, fp32 check)
+    y2 = fpscan.scan_forward(gates, (tokens.float() * 2).to(torch.bfloat16))
+    assert torch.equal(y2, (y.float() * 2).to(torch.bfloat16))
+
+
+def test_config5_2g_elements_fp32():
+    # BASELINE config 5 on one GPU: 4 x 8192 x 65536 fp32 = 2^31 elements
+    # (beyond 32-bit element offsets).  Sampled rows include the last ones.
+    gen = torch.Generator(device=DEVICE).manual_seed(5)
+    shape = (4, 8192, 65536)
+    gates = 0.999 + 0.001 * torch.rand(shape, generator=gen, device=DEVICE)
+    tokens = torch.randn(shape, generator=gen, device=DEVICE) / 65536
+    y = fpscan.scan_forward(gates, tokens)
+    _sample_rows_check(gates, tokens, y, tol=1e-5, seed=5)
+    last = oracle.scan_f64(_np64(gates[-1, -2:]), _np64(tokens[-1, -2:]))
+    assert oracle.normwise_error(_np64(y[-1, -2:]), last) <= 1e-5
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_reverse_equals_flipped_forward(dtype):
+    gates, tokens = _make_inputs(4, 33, 2048, dtype, seed=8)
+    a = fpscan.scan_forward(gates, tokens, reverse=True)
+    b = fpscan.scan_forward(gates.flip(-1).contiguous(), tokens.flip(-1).contiguous()).flip(-1)
+    # same arithmetic in mirrored order: bit-identical
+    assert torch.equal(a, b)
+
+
+# ----------------------------------------------------------------- sequence-shard kernels on one GPU
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("world,L", [(2, 4096), (4, 8192), (8, 65536), (8, 256)])
+def test_seq_shard_kernels_emulated(dtype, world, L):
+    """The shard entry points + carry combine, with ranks emulated in a loop on
+    one GPU (the all-gather replaced by stacking), against the full scan."""
+    from fpscan_b200.distributed import CudaOps
+
+    ops = CudaOps()
+    gates, tokens = _make_inputs(3, 7, L, dtype, seed=L + world)
+    gen = torch.Generator(device=DEVICE).manual_seed(1)
+    go = torch.randn(3, 7, L, generator=gen, device=DEVICE).to(dtype)
+    Lr = L // world
+    sl = [slice(r * Lr, (r + 1) * Lr) for r in range(world)]
+    gs = [gates[..., s].contiguous() for s in sl]
+    xs = [tokens[..., s].contiguous() for s in sl]
+    gos = [go[..., s].contiguous() for s in sl]
+    carries = torch.stack([ops.fwd_reduce(g, x) for g, x in zip(gs, xs)])
+    ys, inits = [], []
+    for r in range(world):
+        init = ops.combine(carries, world, r, reverse=False)
+        inits.append(init)
+        ys.append(ops.fwd_scan_zero(gs[r], xs[r]) if r == 0 else ops.fwd_scan(gs[r], xs[r], init))
+    vs = torch.stack([torch.stack([carries[r, 0], ops.bwd_reduce(gs[r], gos[r])])
+                      for r in range(world)])
+    dgs, dts = [], []
+    for r in range(world):
+        addend = ops.combine(vs, world, r, reverse=True)
+        dg, dt = ops.bwd_scan(gs[r], ys[r], gos[r], addend, inits[r])
+        dgs.append(dg)
+        dts.append(dt)
+    y64 = oracle.scan_f64(_np64(gates), _np64(tokens))
+    dg64, dt64 = oracle.scan_bwd_f64(_np64(gates), y64, _np64(go))
+    _check(torch.cat(ys, -1), y64, dtype, "y")
+    _check(torch.cat(dts, -1), dt64, dtype, "dtokens")
+    _check(torch.cat(dgs, -1), dg64, dtype, "dgates")
+
+
+def test_device_status_clean():
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
