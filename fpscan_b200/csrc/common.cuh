@@ -16,12 +16,11 @@
 
 namespace fpscan {
 
-// Threads per CTA of every streaming kernel; one 16-byte vector per thread per
-// chunk, so a chunk is 4 KiB per tensor whatever the element type.
+// Threads per CTA of every streaming kernel.  Each thread owns NV
+// consecutive 16-byte vectors of a chunk (NV = 1 or 2, a kernel template
+// parameter), so a chunk is kThreads * NV * 16 bytes per tensor.
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kVecBytes = 16;
-constexpr int kChunkBytes = kThreads * kVecBytes;
 
 // Device-side status word.  Bounded waits that give up set a bit here instead
 // of hanging the GPU; the host reads and clears it through
@@ -137,15 +136,54 @@ __device__ __forceinline__ void warp_scan_pair(float& a, float& b, int lane, int
   }
 }
 
-// ---------------------------------------------------------------- launch geometry
-// Rows are processed whole by one CTA ("tile" = consecutive rows).  When a row
-// is shorter than a chunk, a chunk holds several whole rows and the scan is
-// segmented at row boundaries, which fall on thread groups of L/kVec threads.
-struct TileGeom {
-  int64_t rows;           // batch*dim
-  int64_t seqlen;         // L
-  int64_t rows_per_tile;  // rows handled by one CTA
-  int64_t tiles;          // grid size
-};
+// Exclusive per-thread prefix within warp segments of `width` lanes, from
+// the thread's own total (ta, tb): inclusive Hillis-Steele scan, then a
+// shift by one lane.  Leaves the inclusive value in (ta, tb).
+__device__ __forceinline__ void warp_exclusive(float& ta, float& tb, int lane, int width,
+                                               float& ea, float& eb) {
+  warp_scan_pair(ta, tb, lane, width);
+  ea = __shfl_up_sync(0xffffffffu, ta, 1);
+  eb = __shfl_up_sync(0xffffffffu, tb, 1);
+  if ((lane & (width - 1)) == 0) {
+    ea = 1.f;
+    eb = 0.f;
+  }
+}
+
+// Block-level step after the warp scans.  Every warp redundantly scans the
+// kWarps warp totals across its lanes 0..kWarps-1 (segmented in groups of
+// `seg_warps` warps), so no second barrier is needed.
+//   (pa, pb): in = the thread's exclusive prefix within its warp segment,
+//             out = its exclusive prefix within its segment of seg_warps warps;
+//   (ca, cb): the composition of all kWarps totals (the chunk total when one
+//             segment spans the CTA, i.e. seg_warps == kWarps).
+// Compositions start from real operands, never from an identity, so a
+// non-finite A (e.g. an ignored first gate) never meets a 0.
+__device__ __forceinline__ void compose_warp_totals(const float2* wt, int lane, int warp,
+                                                    int seg_warps, float& pa, float& pb,
+                                                    float& ca, float& cb) {
+  float2 t = wt[lane & (kWarps - 1)];
+  const int sl = lane & (seg_warps - 1);
+#pragma unroll
+  for (int d = 1; d < kWarps; d <<= 1) {
+    if (d >= seg_warps) break;
+    const float qa = __shfl_up_sync(0xffffffffu, t.x, d);
+    const float qb = __shfl_up_sync(0xffffffffu, t.y, d);
+    if (sl >= d) {
+      t.y = fmaf(qb, t.x, t.y);
+      t.x = qa * t.x;
+    }
+  }
+  const float wa = __shfl_sync(0xffffffffu, t.x, (warp - 1) & (kWarps - 1));
+  const float wb = __shfl_sync(0xffffffffu, t.y, (warp - 1) & (kWarps - 1));
+  ca = __shfl_sync(0xffffffffu, t.x, kWarps - 1);
+  cb = __shfl_sync(0xffffffffu, t.y, kWarps - 1);
+  if ((warp & (seg_warps - 1)) != 0) {
+    pb = fmaf(wb, pa, pb);
+    pa = wa * pa;
+  }
+}
+
+constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v >> 1); }
 
 }  // namespace fpscan

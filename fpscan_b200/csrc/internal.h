@@ -11,6 +11,12 @@ enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
 
 inline int dtype_size(int dt) { return dt == kF32 ? 4 : 2; }
 
+inline int ilog2_host(int64_t v) {
+  int r = 0;
+  while ((int64_t(1) << (r + 1)) <= v) ++r;
+  return r;
+}
+
 struct FwdArgs {
   const void* gates;
   const void* tokens;
@@ -24,6 +30,7 @@ struct FwdArgs {
   int reverse;
   int num_sms;
   cudaStream_t stream;
+  int nv = 2;           // 16-byte vectors per thread per chunk (1 or 2)
 };
 
 struct BwdArgs {
@@ -40,6 +47,7 @@ struct BwdArgs {
   int dtype;
   int num_sms;
   cudaStream_t stream;
+  int nv = 2;           // 16-byte vectors per thread per chunk (1 or 2)
 };
 
 cudaError_t launch_fwd(const FwdArgs& a);

@@ -12,7 +12,7 @@
 // carries one extra 16-byte vector after the chunk, the y stage one before it,
 // so no global re-reads are needed for the halos.
 //
-// Pipeline, segmentation of short rows and carry handling are the same as in
+// Pipeline, tiling, segmentation of short rows and carry handling follow
 // scan_fwd.cu.  Optional per-row `addend` (value entering at the row's last
 // element, i.e. gates[L] * dtokens[L] of the next sequence shard) and
 // `y_prev` (y before the row's first element, from the previous shard) serve
@@ -23,42 +23,68 @@
 
 namespace fpscan {
 
-constexpr int kBwdStages = 4;
+template <int NV>
+struct BwdCfg {
+  static constexpr int kStages = NV == 1 ? 4 : 3;
+  static constexpr int SV = kThreads * NV;  // 16-byte vectors per chunk
+  static constexpr int GS = SV + 1;         // gates stage: chunk + one vector after
+  static constexpr int YS = SV + 1;         // y stage: one vector before + chunk
+  template <bool HAS_OUT>
+  static constexpr int smem_bytes() {
+    return kStages * 16 * (GS + SV + (HAS_OUT ? YS : 0));
+  }
+};
 
-template <bool HAS_OUT>
-constexpr int bwd_smem_bytes() {
-  return kBwdStages * 16 * ((kThreads + 1) + kThreads + (HAS_OUT ? kThreads + 1 : 0));
-}
+struct BwdKParams {
+  const void* gates;
+  const void* y;
+  const void* gout;
+  void* dgates;
+  void* dtok;
+  const float* addend;
+  const float* y_prev;
+  float* carry_b;
+  int64_t rows;
+  int64_t rows_per_tile;
+  int lg;
+};
 
-template <typename T, bool HAS_OUT, bool HAS_CARRY>
-__global__ void __launch_bounds__(kThreads)
-    scan_bwd_kernel(const T* __restrict__ gates, const T* __restrict__ y,
-                    const T* __restrict__ gout, T* __restrict__ dgates, T* __restrict__ dtok,
-                    const float* __restrict__ addend, const float* __restrict__ y_prev,
-                    float* __restrict__ carry_b, int64_t rows, int64_t L,
-                    int64_t rows_per_tile) {
+template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY>
+__global__ void __launch_bounds__(kThreads) scan_bwd_kernel(const BwdKParams p) {
   constexpr int V = Elem<T>::kVec;
-  constexpr int CH = kThreads * V;
-  constexpr int S = kBwdStages;
-  constexpr int GS = kThreads + 1;  // gates stage: chunk + one vector after
-  constexpr int YS = kThreads + 1;  // y stage: one vector before + chunk
+  constexpr int E = V * NV;
+  constexpr int CH = kThreads * E;
+  constexpr int LGE = ilog2(E);
+  constexpr int LGCH = ilog2(CH);
+  using Cfg = BwdCfg<NV>;
+  constexpr int S = Cfg::kStages;
+  constexpr int SV = Cfg::SV, GS = Cfg::GS, YS = Cfg::YS;
 
   extern __shared__ __align__(128) uint4 dsm[];
-  uint4* s_g = dsm;                    // [S][GS]
-  uint4* s_go = s_g + S * GS;          // [S][kThreads]
-  uint4* s_y = s_go + S * kThreads;    // [S][YS]   (HAS_OUT only)
+  uint4* s_g = dsm;               // [S][GS]
+  uint4* s_go = s_g + S * GS;     // [S][SV]
+  uint4* s_y = s_go + S * SV;     // [S][YS]   (HAS_OUT only)
   __shared__ __align__(8) uint64_t s_bar[S];
-  __shared__ float s_wa[2][kWarps], s_wb[2][kWarps];
+  __shared__ float2 s_wt[2][kWarps];
+
+  const T* __restrict__ gates = static_cast<const T*>(p.gates);
+  const T* __restrict__ y = static_cast<const T*>(p.y);
+  const T* __restrict__ gout = static_cast<const T*>(p.gout);
+  T* __restrict__ dgates = static_cast<T*>(p.dgates);
+  T* __restrict__ dtok = static_cast<T*>(p.dtok);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t row0 = (int64_t)blockIdx.x * rows_per_tile;
-  const int64_t nrows = min(rows_per_tile, rows - row0);
-  const int64_t base = row0 * L;
-  const int64_t n = nrows * L;
-  const int64_t nck = (n + CH - 1) / CH;
+  const int lg = p.lg;
+  const int64_t Lmask = (int64_t(1) << lg) - 1;
+  const int64_t row0 = (int64_t)blockIdx.x * p.rows_per_tile;
+  const int64_t nrows = min(p.rows_per_tile, p.rows - row0);
+  if (nrows <= 0) return;
+  const int64_t base = row0 << lg;
+  const int64_t n = nrows << lg;
+  const int64_t nck = (n + CH - 1) >> LGCH;
 
-  const bool multi = L > CH;
-  const int tpr = multi ? kThreads : (int)(L / V);
+  const bool multi = lg > LGCH;
+  const int tpr = multi ? kThreads : 1 << (lg - LGE);
   const int wwidth = tpr < 32 ? tpr : 32;
   const int seg_warps = tpr >> 5;
 
@@ -72,7 +98,7 @@ __global__ void __launch_bounds__(kThreads)
   int64_t issued = 0;
   auto issue = [&](int64_t k) {
     const int64_t mc = nck - 1 - k;  // reverse processing order
-    const int64_t off = mc * CH;
+    const int64_t off = mc << LGCH;
     const int64_t cnt = min((int64_t)CH, n - off);
     const uint32_t bytes = (uint32_t)(cnt * (int64_t)sizeof(T));
     const uint32_t g_bytes = bytes + ((off + cnt < n) ? 16u : 0u);
@@ -81,7 +107,7 @@ __global__ void __launch_bounds__(kThreads)
     if (HAS_OUT) y_bytes = bytes + (off > 0 ? 16u : 0u);
     mbar_expect_tx(&s_bar[s], g_bytes + bytes + y_bytes);
     bulk_g2s(s_g + s * GS, gates + base + off, g_bytes, &s_bar[s]);
-    bulk_g2s(s_go + s * kThreads, gout + base + off, bytes, &s_bar[s]);
+    bulk_g2s(s_go + s * SV, gout + base + off, bytes, &s_bar[s]);
     if (HAS_OUT) {
       if (off > 0)
         bulk_g2s(s_y + s * YS, y + base + off - V, y_bytes, &s_bar[s]);
@@ -93,37 +119,47 @@ __global__ void __launch_bounds__(kThreads)
     for (; issued < min((int64_t)S, nck); ++issued) issue(issued);
   }
 
-  const int vi = kThreads - 1 - tid;
+  const int vi = kThreads - 1 - tid;  // slot in NV-vector units, reverse order
   const int seg_lane_t = tid & (tpr - 1);
   float carry = 0.f;
   int64_t k = 0;
+  int s = 0;
+  uint32_t phase = 0;
   bool aborted = false;
 
   for (; k < nck; ++k) {
-    const int s = (int)(k % S);
-    const uint32_t parity = (uint32_t)((k / S) & 1);
     const int64_t mc = nck - 1 - k;
-    const int64_t off = mc * CH;
+    const int64_t off = mc << LGCH;
     const int64_t cnt = min((int64_t)CH, n - off);
-    const bool valid = (int64_t)vi * V < cnt;
-    const int64_t vstart = off + (int64_t)vi * V;       // tile-relative first element
-    const bool vec_row_end = ((vstart + V) % L) == 0;   // vector holds a row's last element
-    const bool vec_row_first = (vstart % L) == 0;       // vector holds a row's first element
+    const int64_t vstart = off + ((int64_t)vi << LGE);  // tile-relative first element
+    const bool valid = vstart - off < cnt;
+    const bool grp_row_end = ((vstart + E) & Lmask) == 0;  // holds a row's last element
+    const bool grp_row_first = (vstart & Lmask) == 0;      // holds a row's first element
 
-    const bool ok = mbar_wait_bounded(&s_bar[s], parity);
+    const bool ok = mbar_wait_bounded(&s_bar[s], phase);
 
-    Vec16<T> gv, gov;
-    float g_next = 1.f;
-    float a[V], b[V];
+    Vec16<T> gv[NV], gov[NV], yv[NV];
+    float g_next = 1.f, y_before = 0.f;
+    float a[E], b[E];
     if (valid) {
-      gv.raw = s_g[s * GS + vi];
-      gov.raw = s_go[s * kThreads + vi];
-      if (!vec_row_end) g_next = Elem<T>::load(reinterpret_cast<const T*>(s_g + s * GS + vi + 1)[0]);
+      const uint4* sg = s_g + s * GS + vi * NV;
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
-        const int j = V - 1 - i;
-        const float g = (j == V - 1) ? g_next : Elem<T>::load(gv.e[j + 1]);
-        const float x = Elem<T>::load(gov.e[j]);
+      for (int q = 0; q < NV; ++q) {
+        gv[q].raw = sg[q];
+        gov[q].raw = s_go[s * SV + vi * NV + q];
+      }
+      if (!grp_row_end) g_next = Elem<T>::load(reinterpret_cast<const T*>(sg + NV)[0]);
+      if (HAS_OUT) {
+        const uint4* sy = s_y + s * YS + 1 + vi * NV;
+#pragma unroll
+        for (int q = 0; q < NV; ++q) yv[q].raw = sy[q];
+        if (!grp_row_first) y_before = Elem<T>::load(reinterpret_cast<const T*>(sy)[-1]);
+      }
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const int j = E - 1 - i;  // element within the thread's group, memory order
+        const float g = (j == E - 1) ? g_next : Elem<T>::load(gv[(j + 1) / V].e[(j + 1) % V]);
+        const float x = Elem<T>::load(gov[j / V].e[j % V]);
         if (i == 0) {
           a[0] = g;
           b[0] = x;
@@ -134,34 +170,16 @@ __global__ void __launch_bounds__(kThreads)
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
+      for (int i = 0; i < E; ++i) {
         a[i] = 1.f;
         b[i] = 0.f;
       }
     }
 
-    float ta = a[V - 1], tb = b[V - 1];
-    warp_scan_pair(ta, tb, lane, wwidth);
-    float ea = __shfl_up_sync(0xffffffffu, ta, 1);
-    float eb = __shfl_up_sync(0xffffffffu, tb, 1);
-    if ((lane & (wwidth - 1)) == 0) {
-      ea = 1.f;
-      eb = 0.f;
-    }
-    const int wb_buf = (int)(k & 1);
-    if (lane == 31) {
-      s_wa[wb_buf][warp] = ta;
-      s_wb[wb_buf][warp] = tb;
-    }
-
-    // y values needed for dgates, read before the stage is released.
-    Vec16<T> yv_own;
-    float y_before = 0.f;
-    if (HAS_OUT && valid) {
-      yv_own.raw = s_y[s * YS + vi + 1];
-      if (!vec_row_first)
-        y_before = Elem<T>::load(reinterpret_cast<const T*>(s_y + s * YS + vi + 1)[-1]);
-    }
+    float ta = a[E - 1], tb = b[E - 1], pa, pb;
+    warp_exclusive(ta, tb, lane, wwidth, pa, pb);
+    const int buf = (int)(k & 1);
+    if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
 
     if (__syncthreads_or(!ok)) {
       aborted = true;
@@ -172,30 +190,16 @@ __global__ void __launch_bounds__(kThreads)
       ++issued;
     }
 
-    float wa = 1.f, wbv = 0.f, ca = 1.f, cb = 0.f;
-    if (seg_warps >= 2) {
-      const int first = warp & ~(seg_warps - 1);
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float A = s_wa[wb_buf][w], B = s_wb[wb_buf][w];
-        if (w >= first && w < warp) {
-          wbv = fmaf(wbv, A, B);
-          wa *= A;
-        }
-        cb = fmaf(cb, A, B);
-        ca *= A;
-      }
-    }
-    const float pa = wa * ea;
-    const float pb = fmaf(wbv, ea, eb);
+    float ca = 1.f, cb = 0.f;
+    if (seg_warps >= 2) compose_warp_totals(s_wt[buf], lane, warp, seg_warps, pa, pb, ca, cb);
 
-    const bool row_start = multi ? (((off + CH) % L) == 0) : true;  // processing order
-    const int64_t row = row0 + (multi ? off : vstart) / L;
+    const bool row_start = multi ? (((off + CH) & Lmask) == 0) : true;  // processing order
+    const int64_t row = row0 + ((multi ? off : vstart) >> lg);
     float state;
     bool skip_state = false;
     if (row_start) {
       if (HAS_CARRY) {
-        carry = addend[row];
+        carry = p.addend[row];
         state = fmaf(pa, carry, pb);
       } else {
         carry = 0.f;
@@ -206,30 +210,40 @@ __global__ void __launch_bounds__(kThreads)
       state = fmaf(pa, carry, pb);
     }
 
-    float dt[V];
+    float dt[E];
 #pragma unroll
-    for (int i = 0; i < V; ++i) dt[i] = skip_state ? b[i] : fmaf(a[i], state, b[i]);
+    for (int i = 0; i < E; ++i) dt[i] = skip_state ? b[i] : fmaf(a[i], state, b[i]);
 
     if (valid) {
       if (HAS_OUT) {
         float yp_first = y_before;
-        if (vec_row_first) yp_first = HAS_CARRY ? y_prev[row] : 0.f;
-        Vec16<T> o_dt, o_dg;
+        if (grp_row_first) yp_first = HAS_CARRY ? p.y_prev[row] : 0.f;
+        Vec16<T> o_dt[NV], o_dg[NV];
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-          const int j = V - 1 - i;
-          const float yp = (j == 0) ? yp_first : Elem<T>::load(yv_own.e[j - 1]);
-          o_dt.e[j] = Elem<T>::store(dt[i]);
-          o_dg.e[j] = Elem<T>::store(dt[i] * yp);
+        for (int i = 0; i < E; ++i) {
+          const int j = E - 1 - i;
+          const float yp = (j == 0) ? yp_first : Elem<T>::load(yv[(j - 1) / V].e[(j - 1) % V]);
+          o_dt[j / V].e[j % V] = Elem<T>::store(dt[i]);
+          o_dg[j / V].e[j % V] = Elem<T>::store(dt[i] * yp);
         }
-        reinterpret_cast<uint4*>(dtok + base + off)[vi] = o_dt.raw;
-        reinterpret_cast<uint4*>(dgates + base + off)[vi] = o_dg.raw;
-      } else if (vec_row_first) {
-        carry_b[row] = Elem<T>::load(gv.e[0]) * dt[V - 1];
+        uint4* d1 = reinterpret_cast<uint4*>(dtok + base + off) + vi * NV;
+        uint4* d2 = reinterpret_cast<uint4*>(dgates + base + off) + vi * NV;
+#pragma unroll
+        for (int q = 0; q < NV; ++q) {
+          d1[q] = o_dt[q].raw;
+          d2[q] = o_dg[q].raw;
+        }
+      } else if (grp_row_first) {
+        p.carry_b[row] = Elem<T>::load(gv[0].e[0]) * dt[E - 1];
       }
     }
 
     if (multi) carry = (row_start && !HAS_CARRY) ? cb : fmaf(ca, carry, cb);
+
+    if (++s == S) {
+      s = 0;
+      phase ^= 1u;
+    }
   }
 
   if (aborted && tid == 0) {
@@ -238,37 +252,39 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-template <typename T>
-static int64_t bwd_rows_per_tile(int64_t rows, int64_t L, int num_sms) {
-  constexpr int CH = kThreads * Elem<T>::kVec;
-  int64_t rpt = (8 * (int64_t)CH) / L;
-  const int64_t cap = rows / (4LL * num_sms);
-  if (rpt > cap) rpt = cap;
-  if (rpt < 1) rpt = 1;
-  return rpt;
-}
-
-template <typename T, bool HAS_OUT, bool HAS_CARRY>
+template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY>
 static cudaError_t launch_bwd_t(const BwdArgs& a) {
-  constexpr int smem = bwd_smem_bytes<HAS_OUT>();
-  auto kern = scan_bwd_kernel<T, HAS_OUT, HAS_CARRY>;
-  // Idempotent and cheap; required because the stage ring exceeds 48 KiB.
-  static thread_local int configured_dev = -1;
+  constexpr int smem = BwdCfg<NV>::template smem_bytes<HAS_OUT>();
+  auto kern = scan_bwd_kernel<T, NV, HAS_OUT, HAS_CARRY>;
+  // Per device: opt in to >48 KiB of dynamic shared memory and cache the
+  // number of resident CTAs.
+  static int occ_cache[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (configured_dev != dev) {
+  int occ = (dev >= 0 && dev < 64) ? occ_cache[dev] : 0;
+  if (occ == 0) {
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    configured_dev = dev;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess ||
+        occ < 1)
+      occ = 1;
+    if (dev >= 0 && dev < 64) occ_cache[dev] = occ;
   }
-  const int64_t rpt = bwd_rows_per_tile<T>(a.rows, a.seqlen, a.num_sms);
+  const int64_t slots = (int64_t)a.num_sms * occ;
+  int64_t rpt = (a.rows + slots - 1) / slots;
+  if (rpt < 1) rpt = 1;
   const int64_t tiles = (a.rows + rpt - 1) / rpt;
-  kern<<<(unsigned)tiles, kThreads, smem, a.stream>>>(
-      static_cast<const T*>(a.gates), static_cast<const T*>(a.y),
-      static_cast<const T*>(a.grad_out), static_cast<T*>(a.dgates), static_cast<T*>(a.dtokens),
-      a.addend, a.y_prev, a.carry_b, a.rows, a.seqlen, rpt);
+  BwdKParams p{a.gates, a.y, a.grad_out, a.dgates, a.dtokens, a.addend, a.y_prev, a.carry_b,
+               a.rows, rpt, ilog2_host(a.seqlen)};
+  kern<<<(unsigned)tiles, kThreads, smem, a.stream>>>(p);
   return cudaGetLastError();
+}
+
+template <typename T, bool HAS_OUT, bool HAS_CARRY>
+static cudaError_t launch_bwd_nv(const BwdArgs& a) {
+  return a.nv == 1 ? launch_bwd_t<T, 1, HAS_OUT, HAS_CARRY>(a)
+                   : launch_bwd_t<T, 2, HAS_OUT, HAS_CARRY>(a);
 }
 
 template <typename T>
@@ -276,8 +292,8 @@ static cudaError_t launch_bwd_dtype(const BwdArgs& a) {
   const bool has_out = a.dtokens != nullptr;
   const bool has_carry = a.addend != nullptr;
   if (has_out)
-    return has_carry ? launch_bwd_t<T, true, true>(a) : launch_bwd_t<T, true, false>(a);
-  return has_carry ? launch_bwd_t<T, false, true>(a) : launch_bwd_t<T, false, false>(a);
+    return has_carry ? launch_bwd_nv<T, true, true>(a) : launch_bwd_nv<T, true, false>(a);
+  return launch_bwd_nv<T, false, false>(a);
 }
 
 cudaError_t launch_bwd(const BwdArgs& a) {

@@ -3,18 +3,21 @@
 //
 // Replaces the reference kernel scan<> (csrc/full_scan/full_scan.cu:50-177)
 // with a different design:
-//   * one CTA streams a tile of whole rows, chunk by chunk (4 KiB per tensor
-//     per chunk), through a kStages-deep shared-memory ring filled by
-//     non-multicast cp.async.bulk copies completing on mbarriers, so several
-//     chunks per CTA are in flight while the current one is scanned;
-//   * per-thread serial scan over one 16-byte vector (4 fp32 / 8 half),
-//     warp-shuffle Hillis-Steele scan of the thread totals, then a
-//     per-warp redundant composition of the (double-buffered) warp totals --
-//     one __syncthreads per chunk;
+//   * one CTA streams a tile of whole consecutive rows, chunk by chunk, through
+//     a kStages-deep shared-memory ring filled by non-multicast cp.async.bulk
+//     copies completing on mbarriers; the grid is one wave (tiles =
+//     SMs x resident CTAs), so each CTA's pipeline runs across row boundaries
+//     without draining;
+//   * each thread owns NV consecutive 16-byte vectors of a chunk (4*NV fp32 or
+//     8*NV half values): in-register serial scan, warp-shuffle Hillis-Steele
+//     scan of the thread totals, then a lane-parallel scan of the
+//     (double-buffered) warp totals done redundantly by every warp -- one
+//     __syncthreads per chunk;
 //   * rows shorter than a chunk are packed several to a chunk and scanned as
 //     independent segments (row boundaries coincide with power-of-two thread
-//     groups), rows longer than a chunk carry their fp32 state across chunks;
-//   * 64-bit offsets throughout; any number of rows (no gridDim.y limit).
+//     groups); rows longer than a chunk carry their fp32 state across chunks;
+//   * 64-bit offsets, shifts and masks only (seqlen is a power of two); any
+//     number of rows.
 // Optional per-row initial state (`init`) and per-row carry-out
 // (A = product of all gates of the row, B = final state) serve the
 // sequence-sharded multi-GPU mode.  Without `init` the gate of a row's first
@@ -25,34 +28,59 @@
 
 namespace fpscan {
 
-constexpr int kFwdStages = 4;
+template <int NV>
+struct FwdCfg {
+  static constexpr int kStages = NV == 1 ? 4 : 3;
+  static constexpr int SV = kThreads * NV;  // 16-byte vectors per chunk
+  static constexpr int smem_bytes() { return kStages * 2 * SV * 16; }
+};
 
-template <typename T, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
-__global__ void __launch_bounds__(kThreads)
-    scan_fwd_kernel(const T* __restrict__ gates, const T* __restrict__ tokens, T* out,
-                    const float* __restrict__ init, float* __restrict__ carry_a,
-                    float* __restrict__ carry_b, int64_t rows, int64_t L,
-                    int64_t rows_per_tile) {
-  constexpr int V = Elem<T>::kVec;
-  constexpr int CH = kThreads * V;  // elements per chunk
-  constexpr int S = kFwdStages;
+struct FwdKParams {
+  const void* gates;
+  const void* tokens;
+  void* out;
+  const float* init;
+  float* carry_a;
+  float* carry_b;
+  int64_t rows;
+  int64_t rows_per_tile;
+  int lg;  // log2(seqlen)
+};
 
-  __shared__ __align__(128) uint4 s_g[S][kThreads];
-  __shared__ __align__(128) uint4 s_x[S][kThreads];
+template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
+__global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdKParams p) {
+  constexpr int V = Elem<T>::kVec;   // elements per 16-byte vector
+  constexpr int E = V * NV;          // elements per thread per chunk
+  constexpr int CH = kThreads * E;   // elements per chunk
+  constexpr int LGE = ilog2(E);
+  constexpr int LGCH = ilog2(CH);
+  constexpr int S = FwdCfg<NV>::kStages;
+  constexpr int SV = FwdCfg<NV>::SV;
+
+  extern __shared__ __align__(128) uint4 dsm[];
+  uint4 (*s_g)[SV] = reinterpret_cast<uint4 (*)[SV]>(dsm);           // [S][SV]
+  uint4 (*s_x)[SV] = reinterpret_cast<uint4 (*)[SV]>(dsm + S * SV);  // [S][SV]
   __shared__ __align__(8) uint64_t s_bar[S];
-  __shared__ float s_wa[2][kWarps], s_wb[2][kWarps];
+  __shared__ float2 s_wt[2][kWarps];
+
+  const T* __restrict__ gates = static_cast<const T*>(p.gates);
+  const T* __restrict__ tokens = static_cast<const T*>(p.tokens);
+  T* out = static_cast<T*>(p.out);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t row0 = (int64_t)blockIdx.x * rows_per_tile;
-  const int64_t nrows = min(rows_per_tile, rows - row0);
-  const int64_t base = row0 * L;
-  const int64_t n = nrows * L;
-  const int64_t nck = (n + CH - 1) / CH;
+  const int lg = p.lg;
+  const int64_t Lmask = (int64_t(1) << lg) - 1;
+  const int64_t row0 = (int64_t)blockIdx.x * p.rows_per_tile;
+  const int64_t nrows = min(p.rows_per_tile, p.rows - row0);
+  if (nrows <= 0) return;
+  const int64_t base = row0 << lg;
+  const int64_t n = nrows << lg;
+  const int64_t nck = (n + CH - 1) >> LGCH;
 
-  const bool multi = L > CH;  // a row spans several chunks
-  const int tpr = multi ? kThreads : (int)(L / V);  // threads per segment (power of two)
+  const bool multi = lg > LGCH;                        // a row spans several chunks
+  const int tpr = multi ? kThreads : 1 << (lg - LGE);  // threads per segment
   const int wwidth = tpr < 32 ? tpr : 32;
-  const int seg_warps = tpr >> 5;  // warps per segment, 0 if sub-warp
+  const int seg_warps = tpr >> 5;
 
   if (tid == 0) {
 #pragma unroll
@@ -61,10 +89,11 @@ __global__ void __launch_bounds__(kThreads)
   }
   __syncthreads();
 
-  int64_t issued = 0;  // meaningful in thread 0 only
+  // Thread 0 issues chunk loads; `issued` counts them.
+  int64_t issued = 0;
   auto issue = [&](int64_t k) {
     const int64_t mc = REV ? nck - 1 - k : k;
-    const int64_t off = mc * CH;
+    const int64_t off = mc << LGCH;
     const int64_t cnt = min((int64_t)CH, n - off);
     const uint32_t bytes = (uint32_t)(cnt * (int64_t)sizeof(T));
     const int s = (int)(k % S);
@@ -76,33 +105,36 @@ __global__ void __launch_bounds__(kThreads)
     for (; issued < min((int64_t)S, nck); ++issued) issue(issued);
   }
 
-  const int vi = REV ? kThreads - 1 - tid : tid;  // vector slot in the chunk
-  const int seg_lane_t = tid & (tpr - 1);          // thread index in its segment
+  const int vi = REV ? kThreads - 1 - tid : tid;  // thread's slot (in NV-vector units)
+  const int seg_lane_t = tid & (tpr - 1);          // thread index within its segment
   float carry = 0.f;  // state entering the current chunk (multi-chunk rows)
-  float acc_a = 1.f;  // running gate product of the current row (multi-chunk rows)
+  float acc_a = 1.f;  // gate product of the current row so far (multi-chunk rows)
   int64_t k = 0;
+  int s = 0;
+  uint32_t phase = 0;
   bool aborted = false;
 
   for (; k < nck; ++k) {
-    const int s = (int)(k % S);
-    const uint32_t parity = (uint32_t)((k / S) & 1);
     const int64_t mc = REV ? nck - 1 - k : k;
-    const int64_t off = mc * CH;
+    const int64_t off = mc << LGCH;
     const int64_t cnt = min((int64_t)CH, n - off);
-    const bool valid = (int64_t)vi * V < cnt;
+    const bool valid = ((int64_t)vi << LGE) < cnt;
 
-    const bool ok = mbar_wait_bounded(&s_bar[s], parity);
+    const bool ok = mbar_wait_bounded(&s_bar[s], phase);
 
-    float a[V], b[V];
+    float a[E], b[E];
     if (valid) {
-      Vec16<T> gv, xv;
-      gv.raw = s_g[s][vi];
-      xv.raw = s_x[s][vi];
+      Vec16<T> gv[NV], xv[NV];
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
-        const int j = REV ? V - 1 - i : i;
-        const float g = Elem<T>::load(gv.e[j]);
-        const float x = Elem<T>::load(xv.e[j]);
+      for (int q = 0; q < NV; ++q) {
+        gv[q].raw = s_g[s][vi * NV + q];
+        xv[q].raw = s_x[s][vi * NV + q];
+      }
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const int j = REV ? E - 1 - i : i;
+        const float g = Elem<T>::load(gv[j / V].e[j % V]);
+        const float x = Elem<T>::load(xv[j / V].e[j % V]);
         if (i == 0) {
           a[0] = g;
           b[0] = x;
@@ -113,27 +145,17 @@ __global__ void __launch_bounds__(kThreads)
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
+      for (int i = 0; i < E; ++i) {
         a[i] = 1.f;
         b[i] = 0.f;
       }
     }
 
-    // Inclusive scan of thread totals within the warp segment, then the
-    // exclusive prefix of this thread.
-    float ta = a[V - 1], tb = b[V - 1];
-    warp_scan_pair(ta, tb, lane, wwidth);
-    float ea = __shfl_up_sync(0xffffffffu, ta, 1);
-    float eb = __shfl_up_sync(0xffffffffu, tb, 1);
-    if ((lane & (wwidth - 1)) == 0) {
-      ea = 1.f;
-      eb = 0.f;
-    }
-    const int wb_buf = (int)(k & 1);
-    if (lane == 31) {
-      s_wa[wb_buf][warp] = ta;
-      s_wb[wb_buf][warp] = tb;
-    }
+    float ta = a[E - 1], tb = b[E - 1], pa, pb;
+    warp_exclusive(ta, tb, lane, wwidth, pa, pb);
+    const int buf = (int)(k & 1);
+    if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
+
     if (__syncthreads_or(!ok)) {
       aborted = true;
       break;
@@ -144,33 +166,17 @@ __global__ void __launch_bounds__(kThreads)
       ++issued;
     }
 
-    // Prefix of the warps before this one in the segment, and (multi-chunk
-    // rows) the composition of the whole chunk.
-    float wa = 1.f, wbv = 0.f, ca = 1.f, cb = 0.f;
-    if (seg_warps >= 2) {
-      const int first = warp & ~(seg_warps - 1);
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float A = s_wa[wb_buf][w], B = s_wb[wb_buf][w];
-        if (w >= first && w < warp) {
-          wbv = fmaf(wbv, A, B);
-          wa *= A;
-        }
-        cb = fmaf(cb, A, B);
-        ca *= A;
-      }
-    }
-    const float pa = wa * ea;
-    const float pb = fmaf(wbv, ea, eb);
+    float ca = 1.f, cb = 0.f;
+    if (seg_warps >= 2) compose_warp_totals(s_wt[buf], lane, warp, seg_warps, pa, pb, ca, cb);
 
     // Does this chunk start its row (in processing order)?
-    const bool row_start = multi ? (((REV ? off + CH : off) % L) == 0) : true;
-    const int64_t row = row0 + (multi ? off : off + (int64_t)vi * V) / L;
+    const bool row_start = multi ? (((REV ? off + CH : off) & Lmask) == 0) : true;
+    const int64_t row = row0 + ((multi ? off : off + ((int64_t)vi << LGE)) >> lg);
     float state;  // y just before this thread's first element
     bool skip_state = false;
     if (row_start) {
       if (HAS_INIT) {
-        carry = init[row];
+        carry = p.init[row];
         state = fmaf(pa, carry, pb);
       } else {
         carry = 0.f;
@@ -181,28 +187,38 @@ __global__ void __launch_bounds__(kThreads)
       state = fmaf(pa, carry, pb);
     }
 
-    float yv[V];
+    float yv[E];
 #pragma unroll
-    for (int i = 0; i < V; ++i) yv[i] = skip_state ? b[i] : fmaf(a[i], state, b[i]);
+    for (int i = 0; i < E; ++i) yv[i] = skip_state ? b[i] : fmaf(a[i], state, b[i]);
 
     if (HAS_OUT && valid) {
-      Vec16<T> ov;
+      Vec16<T> ov[NV];
 #pragma unroll
-      for (int i = 0; i < V; ++i) ov.e[REV ? V - 1 - i : i] = Elem<T>::store(yv[i]);
-      reinterpret_cast<uint4*>(out + base + off)[vi] = ov.raw;
+      for (int i = 0; i < E; ++i) {
+        const int j = REV ? E - 1 - i : i;
+        ov[j / V].e[j % V] = Elem<T>::store(yv[i]);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out + base + off) + vi * NV;
+#pragma unroll
+      for (int q = 0; q < NV; ++q) dst[q] = ov[q].raw;
     }
 
     if (multi) {
       const float new_carry = (row_start && !HAS_INIT) ? cb : fmaf(ca, carry, cb);
       acc_a = (row_start ? 1.f : acc_a) * ca;
       carry = new_carry;
-      if (HAS_CARRY_OUT && tid == 0 && ((REV ? off : off + CH) % L) == 0) {
-        carry_a[row] = acc_a;
-        carry_b[row] = carry;
+      if (HAS_CARRY_OUT && tid == 0 && ((REV ? off : off + CH) & Lmask) == 0) {
+        p.carry_a[row] = acc_a;
+        p.carry_b[row] = carry;
       }
     } else if (HAS_CARRY_OUT && valid && seg_lane_t == tpr - 1) {
-      carry_a[row] = pa * a[V - 1];
-      carry_b[row] = yv[V - 1];
+      p.carry_a[row] = pa * a[E - 1];
+      p.carry_b[row] = yv[E - 1];
+    }
+
+    if (++s == S) {
+      s = 0;
+      phase ^= 1u;
     }
   }
 
@@ -214,27 +230,39 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-template <typename T>
-static int64_t pick_rows_per_tile(int64_t rows, int64_t L, int num_sms) {
-  constexpr int CH = kThreads * Elem<T>::kVec;
-  const int64_t target = 8 * (int64_t)CH;  // ~32 KiB of each tensor per CTA
-  int64_t rpt = target / L;
-  const int64_t min_tiles = 4LL * num_sms;
-  const int64_t cap = rows / min_tiles;
-  if (rpt > cap) rpt = cap;
+// One wave of CTAs: tiles = SMs x resident CTAs per SM (queried once per
+// device and kernel), each a contiguous run of whole rows.
+template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
+static cudaError_t launch_fwd_t(const FwdArgs& a) {
+  constexpr int smem = FwdCfg<NV>::smem_bytes();
+  auto kern = scan_fwd_kernel<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>;
+  static int occ_cache[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  int occ = (dev >= 0 && dev < 64) ? occ_cache[dev] : 0;
+  if (occ == 0) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem) != cudaSuccess ||
+        occ < 1)
+      occ = 1;
+    if (dev >= 0 && dev < 64) occ_cache[dev] = occ;
+  }
+  const int64_t slots = (int64_t)a.num_sms * occ;
+  int64_t rpt = (a.rows + slots - 1) / slots;
   if (rpt < 1) rpt = 1;
-  return rpt;
+  const int64_t tiles = (a.rows + rpt - 1) / rpt;
+  FwdKParams p{a.gates, a.tokens, a.out, a.init, a.carry_a, a.carry_b, a.rows, rpt,
+               ilog2_host(a.seqlen)};
+  kern<<<(unsigned)tiles, kThreads, smem, a.stream>>>(p);
+  return cudaGetLastError();
 }
 
 template <typename T, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
-static cudaError_t launch_fwd_t(const FwdArgs& a) {
-  const int64_t rpt = pick_rows_per_tile<T>(a.rows, a.seqlen, a.num_sms);
-  const int64_t tiles = (a.rows + rpt - 1) / rpt;
-  scan_fwd_kernel<T, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>
-      <<<(unsigned)tiles, kThreads, 0, a.stream>>>(
-          static_cast<const T*>(a.gates), static_cast<const T*>(a.tokens),
-          static_cast<T*>(a.out), a.init, a.carry_a, a.carry_b, a.rows, a.seqlen, rpt);
-  return cudaGetLastError();
+static cudaError_t launch_fwd_nv(const FwdArgs& a) {
+  return a.nv == 1 ? launch_fwd_t<T, 1, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>(a)
+                   : launch_fwd_t<T, 2, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>(a);
 }
 
 template <typename T>
@@ -242,26 +270,16 @@ static cudaError_t launch_fwd_dtype(const FwdArgs& a) {
   const bool has_out = a.out != nullptr;
   const bool has_init = a.init != nullptr;
   const bool has_co = a.carry_a != nullptr;
-  // Instantiated variants: plain scan (fwd/rev), scan with init (+carry-out),
-  // carry-out only (reduce).
+  // Instantiated variants: plain scan (fwd/rev); forward with init
+  // (+carry-out); carry-out only (reduce).
   if (has_out && !has_init && !has_co)
-    return a.reverse ? launch_fwd_t<T, true, true, false, false>(a)
-                     : launch_fwd_t<T, false, true, false, false>(a);
-  if (has_out && has_init && !has_co)
-    return a.reverse ? launch_fwd_t<T, true, true, true, false>(a)
-                     : launch_fwd_t<T, false, true, true, false>(a);
-  if (has_out && has_init && has_co)
-    return a.reverse ? launch_fwd_t<T, true, true, true, true>(a)
-                     : launch_fwd_t<T, false, true, true, true>(a);
-  if (has_out && !has_init && has_co)
-    return a.reverse ? launch_fwd_t<T, true, true, false, true>(a)
-                     : launch_fwd_t<T, false, true, false, true>(a);
-  if (!has_out && !has_init && has_co)
-    return a.reverse ? launch_fwd_t<T, true, false, false, true>(a)
-                     : launch_fwd_t<T, false, false, false, true>(a);
-  if (!has_out && has_init && has_co)
-    return a.reverse ? launch_fwd_t<T, true, false, true, true>(a)
-                     : launch_fwd_t<T, false, false, true, true>(a);
+    return a.reverse ? launch_fwd_nv<T, true, true, false, false>(a)
+                     : launch_fwd_nv<T, false, true, false, false>(a);
+  if (a.reverse) return cudaErrorInvalidValue;
+  if (has_out && has_init && !has_co) return launch_fwd_nv<T, false, true, true, false>(a);
+  if (has_out && has_init && has_co) return launch_fwd_nv<T, false, true, true, true>(a);
+  if (has_out && !has_init && has_co) return launch_fwd_nv<T, false, true, false, true>(a);
+  if (!has_out && !has_init && has_co) return launch_fwd_nv<T, false, false, false, true>(a);
   return cudaErrorInvalidValue;
 }
 

@@ -196,6 +196,7 @@ def test_first_gate_is_ignored_like_reference():
     g = _np64(gates)
     g[..., 0] = 0.0
     _check(out, oracle.scan_f64(g, _np64(tokens)), torch.float32)
+    gates, tokens = _make_inputs(2, 3, 4096, torch.float32, seed=2)
     gates[..., -1] = float("nan")
     out = fpscan.scan_forward(gates, tokens, reverse=True)
     g = _np64(gates)
