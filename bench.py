@@ -46,8 +46,10 @@ CONFIGS = {
 }
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the backward
-# kernel from ncu (profiles/scan_bwd_bf16_cfg4.md); None until captured.
-NCU_TRAFFIC_BYTES = {}
+# kernel, from one ncu capture (profiles/scan_fwd_bwd_bf16_cfg3_full.md) of
+# config 3 (134.2M elements: 1297.0 MB), scaled by the element count to the
+# config-4 launch of each rank (traffic grows in proportion to the rows).
+_CFG3_BWD_TRAFFIC_PER_ELEM = 1297.0e6 / (8 * 2048 * 8192)
 
 
 def _peaks():
@@ -320,7 +322,8 @@ def run_fpscan(args, cfg):
     fwd_mean = statistics.mean(fwd_ms)
     achieved_bwd = 5 * n_local * s / (bwd_mean / 1e3) / 1e9
     achieved_fwd = 3 * n_local * s / (fwd_mean / 1e3) / 1e9
-    traffic = NCU_TRAFFIC_BYTES.get((args.config, world))
+    traffic = (int(_CFG3_BWD_TRAFFIC_PER_ELEM * n_local)
+               if cfg["dtype"] in ("bfloat16", "float16") else None)
 
     e2e = None
     if not args.no_e2e:

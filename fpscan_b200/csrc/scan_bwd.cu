@@ -50,7 +50,7 @@ struct BwdKParams {
 };
 
 template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY>
-__global__ void __launch_bounds__(kThreads) scan_bwd_kernel(const BwdKParams p) {
+__global__ void __launch_bounds__(kThreads, 3) scan_bwd_kernel(const BwdKParams p) {
   constexpr int V = Elem<T>::kVec;
   constexpr int E = V * NV;
   constexpr int CH = kThreads * E;

@@ -48,7 +48,7 @@ struct FwdKParams {
 };
 
 template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
-__global__ void __launch_bounds__(kThreads) scan_fwd_kernel(const FwdKParams p) {
+__global__ void __launch_bounds__(kThreads, 4) scan_fwd_kernel(const FwdKParams p) {
   constexpr int V = Elem<T>::kVec;   // elements per 16-byte vector
   constexpr int E = V * NV;          // elements per thread per chunk
   constexpr int CH = kThreads * E;   // elements per chunk
