@@ -54,12 +54,14 @@ def needs_build() -> bool:
     return any(os.path.getmtime(p) > t for p in _deps())
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> str:
-    """Compile the library if needed; returns its path."""
-    if not force and not needs_build():
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False,
+          defines=(), out_path: str = LIB_PATH) -> str:
+    """Compile the library if needed; returns its path.  `defines` (-D flags)
+    and `out_path` build an alternative variant elsewhere (always rebuilt)."""
+    if out_path == LIB_PATH and not defines and not force and not needs_build():
         return LIB_PATH
     nvcc = _nvcc()
-    extra = ["-Xptxas", "-v"] if ptxas_verbose else []
+    extra = (["-Xptxas", "-v"] if ptxas_verbose else []) + [f"-D{d}" for d in defines]
     with tempfile.TemporaryDirectory(prefix="fpscan_build_") as tmp:
         objs = []
         procs = []
@@ -87,8 +89,9 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         if verbose:
             print(" ".join(cmd))
         subprocess.run(cmd, check=True)
-        os.replace(tmp_lib, LIB_PATH)
-    return LIB_PATH
+        os.makedirs(os.path.dirname(out_path), exist_ok=True)
+        os.replace(tmp_lib, out_path)
+    return out_path
 
 
 if __name__ == "__main__":

@@ -103,14 +103,21 @@ int cuda_result(cudaError_t e, const char* what) {
 }
 
 // Vectors per thread per chunk.  2 (default) amortises the per-chunk scan and
-// barrier over twice the data; FPSCAN_B200_NV=1 selects the one-vector
-// variant (a tuning knob read once per process).
-int tuned_nv() {
-  static const int nv = [] {
+// barrier over twice the data; FPSCAN_B200_NV=1 / =4 select the one- and
+// (fp32 only) four-vector variants (a tuning knob read once per process).
+// Measured defaults on B200 (config 4, 1.3 G elements): the forward scan of
+// half types is fastest with 1 vector per thread (more resident CTAs), every
+// other case with 2.
+int tuned_nv(bool forward, int dtype) {
+  static const int env = [] {
     const char* v = getenv("FPSCAN_B200_NV");
-    return (v && v[0] == '1') ? 1 : 2;
+    if (v && v[0] == '1') return 1;
+    if (v && v[0] == '2') return 2;
+    if (v && v[0] == '4') return 4;  // fp32 only; other types use 2
+    return 0;
   }();
-  return nv;
+  if (env) return env;
+  return (forward && dtype != kF32) ? 1 : 2;
 }
 
 constexpr int64_t kRefMinL = 32, kRefMaxL = 65536;  // csrc/full_scan/full_scan.cu:207-233
@@ -151,7 +158,7 @@ int fpscan_scan_fwd(const void* gates, const void* tokens, void* out, int64_t ba
       return fail(FPSCAN_ERR_INVALID, "out partially overlaps %s", in->name);
   FwdArgs a{gates, tokens, out, nullptr, nullptr, nullptr, rows, seqlen, dtype,
             reverse ? 1 : 0, num_sms_current(), static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv();
+  a.nv = tuned_nv(true, dtype);
   return cuda_result(launch_fwd(a), "fpscan_scan_fwd launch");
 }
 
@@ -180,7 +187,7 @@ int fpscan_scan_bwd(const void* gates, const void* y, const void* grad_out, void
   BwdArgs a{gates,   y,       grad_out, dgates, dtokens, nullptr, nullptr,
             nullptr, rows,    seqlen,   dtype,  num_sms_current(),
             static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv();
+  a.nv = tuned_nv(false, dtype);
   return cuda_result(launch_bwd(a), "fpscan_scan_bwd launch");
 }
 
@@ -196,7 +203,7 @@ int fpscan_shard_fwd_reduce(const void* gates, const void* tokens, float* carry_
   if (!carry_a || !carry_b) return fail(FPSCAN_ERR_INVALID, "carry_a/carry_b is NULL");
   FwdArgs a{gates, tokens, nullptr, nullptr, carry_a, carry_b, r, seqlen, dtype, 0,
             num_sms_current(), static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv();
+  a.nv = tuned_nv(true, dtype);
   return cuda_result(launch_fwd(a), "fpscan_shard_fwd_reduce launch");
 }
 
@@ -212,7 +219,7 @@ int fpscan_shard_fwd_scan(const void* gates, const void* tokens, void* out, cons
   if (!y_init) return fail(FPSCAN_ERR_INVALID, "y_init is NULL");
   FwdArgs a{gates, tokens, out, y_init, nullptr, nullptr, r, seqlen, dtype, 0,
             num_sms_current(), static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv();
+  a.nv = tuned_nv(true, dtype);
   return cuda_result(launch_fwd(a), "fpscan_shard_fwd_scan launch");
 }
 
@@ -228,7 +235,7 @@ int fpscan_shard_bwd_reduce(const void* gates, const void* grad_out, float* carr
   BwdArgs a{gates,   nullptr, grad_out, nullptr, nullptr, nullptr, nullptr,
             carry_b, r,       seqlen,   dtype,   num_sms_current(),
             static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv();
+  a.nv = tuned_nv(false, dtype);
   return cuda_result(launch_bwd(a), "fpscan_shard_bwd_reduce launch");
 }
 
@@ -248,7 +255,7 @@ int fpscan_shard_bwd_scan(const void* gates, const void* y, const void* grad_out
   BwdArgs a{gates,   y, grad_out, dgates, dtokens, addend, y_prev,
             nullptr, r, seqlen,   dtype,  num_sms_current(),
             static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv();
+  a.nv = tuned_nv(false, dtype);
   return cuda_result(launch_bwd(a), "fpscan_shard_bwd_scan launch");
 }
 

@@ -184,6 +184,47 @@ __device__ __forceinline__ void compose_warp_totals(const float2* wt, int lane, 
   }
 }
 
+// Loads a thread's NV consecutive 16-byte vectors from shared memory.
+// (A bank-conflict-free swizzled order was measured slower: the selects it
+// needs cost more issue slots than the 2-way conflicts of this order.)
+template <int NV>
+__device__ __forceinline__ void lds_vecs(const uint4* src, uint4 (&r)[NV]) {
+#pragma unroll
+  for (int q = 0; q < NV; ++q) r[q] = src[q];
+}
+
+// Packs fp32 values into one 16-byte vector of T with paired conversions
+// (one cvt for two half values).
+template <typename T>
+__device__ __forceinline__ uint4 pack_vec(const float* v);
+template <>
+__device__ __forceinline__ uint4 pack_vec<float>(const float* v) {
+  return make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                    __float_as_uint(v[3]));
+}
+template <>
+__device__ __forceinline__ uint4 pack_vec<__nv_bfloat16>(const float* v) {
+  uint4 r;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return r;
+}
+template <>
+__device__ __forceinline__ uint4 pack_vec<__half>(const float* v) {
+  uint4 r;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return r;
+}
+
 constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v >> 1); }
 
 }  // namespace fpscan

@@ -25,7 +25,8 @@ namespace fpscan {
 
 template <int NV>
 struct BwdCfg {
-  static constexpr int kStages = NV == 1 ? 4 : 3;
+  static constexpr int kStages = NV == 1 ? 4 : (NV == 2 ? 3 : 2);
+  static constexpr int kMinBlocks = NV == 4 ? 2 : 3;  // resident CTAs the smem ring allows
   static constexpr int SV = kThreads * NV;  // 16-byte vectors per chunk
   static constexpr int GS = SV + 1;         // gates stage: chunk + one vector after
   static constexpr int YS = SV + 1;         // y stage: one vector before + chunk
@@ -50,7 +51,7 @@ struct BwdKParams {
 };
 
 template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY>
-__global__ void __launch_bounds__(kThreads, 3) scan_bwd_kernel(const BwdKParams p) {
+__global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks) scan_bwd_kernel(const BwdKParams p) {
   constexpr int V = Elem<T>::kVec;
   constexpr int E = V * NV;
   constexpr int CH = kThreads * E;
@@ -141,20 +142,31 @@ __global__ void __launch_bounds__(kThreads, 3) scan_bwd_kernel(const BwdKParams 
     Vec16<T> gv[NV], gov[NV], yv[NV];
     float g_next = 1.f, y_before = 0.f;
     float a[E], b[E];
-    if (valid) {
+    {
+      // Halo elements: gates[vstart+E] (first gate of the next slot) and
+      // y[vstart-1] (last y of the previous slot).
+      uint4 rg[NV], rgo[NV], ry[NV];
       const uint4* sg = s_g + s * GS + vi * NV;
+      const uint4* sy = s_y + s * YS + 1 + vi * NV;
+      if (valid) {
+        lds_vecs<NV>(sg, rg);
+        lds_vecs<NV>(s_go + s * SV + vi * NV, rgo);
+        if (HAS_OUT) lds_vecs<NV>(sy, ry);
+      } else {
+#pragma unroll
+        for (int q = 0; q < NV; ++q) rg[q] = rgo[q] = ry[q] = make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
       for (int q = 0; q < NV; ++q) {
-        gv[q].raw = sg[q];
-        gov[q].raw = s_go[s * SV + vi * NV + q];
+        gv[q].raw = rg[q];
+        gov[q].raw = rgo[q];
+        if (HAS_OUT) yv[q].raw = ry[q];
       }
-      if (!grp_row_end) g_next = Elem<T>::load(reinterpret_cast<const T*>(sg + NV)[0]);
-      if (HAS_OUT) {
-        const uint4* sy = s_y + s * YS + 1 + vi * NV;
-#pragma unroll
-        for (int q = 0; q < NV; ++q) yv[q].raw = sy[q];
-        if (!grp_row_first) y_before = Elem<T>::load(reinterpret_cast<const T*>(sy)[-1]);
-      }
+      if (valid && !grp_row_end) g_next = Elem<T>::load(reinterpret_cast<const T*>(sg + NV)[0]);
+      if (HAS_OUT && valid && !grp_row_first)
+        y_before = Elem<T>::load(reinterpret_cast<const T*>(sy)[-1]);
+    }
+    if (valid) {
 #pragma unroll
       for (int i = 0; i < E; ++i) {
         const int j = E - 1 - i;  // element within the thread's group, memory order
@@ -218,20 +230,20 @@ __global__ void __launch_bounds__(kThreads, 3) scan_bwd_kernel(const BwdKParams 
       if (HAS_OUT) {
         float yp_first = y_before;
         if (grp_row_first) yp_first = HAS_CARRY ? p.y_prev[row] : 0.f;
-        Vec16<T> o_dt[NV], o_dg[NV];
+        float f_dt[E], f_dg[E];  // memory order
 #pragma unroll
         for (int i = 0; i < E; ++i) {
           const int j = E - 1 - i;
           const float yp = (j == 0) ? yp_first : Elem<T>::load(yv[(j - 1) / V].e[(j - 1) % V]);
-          o_dt[j / V].e[j % V] = Elem<T>::store(dt[i]);
-          o_dg[j / V].e[j % V] = Elem<T>::store(dt[i] * yp);
+          f_dt[j] = dt[i];
+          f_dg[j] = dt[i] * yp;
         }
         uint4* d1 = reinterpret_cast<uint4*>(dtok + base + off) + vi * NV;
         uint4* d2 = reinterpret_cast<uint4*>(dgates + base + off) + vi * NV;
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
-          d1[q] = o_dt[q].raw;
-          d2[q] = o_dg[q].raw;
+          d1[q] = pack_vec<T>(f_dt + q * V);
+          d2[q] = pack_vec<T>(f_dg + q * V);
         }
       } else if (grp_row_first) {
         p.carry_b[row] = Elem<T>::load(gv[0].e[0]) * dt[E - 1];
@@ -283,6 +295,8 @@ static cudaError_t launch_bwd_t(const BwdArgs& a) {
 
 template <typename T, bool HAS_OUT, bool HAS_CARRY>
 static cudaError_t launch_bwd_nv(const BwdArgs& a) {
+  if constexpr (sizeof(T) == 4)
+    if (a.nv == 4) return launch_bwd_t<T, 4, HAS_OUT, HAS_CARRY>(a);
   return a.nv == 1 ? launch_bwd_t<T, 1, HAS_OUT, HAS_CARRY>(a)
                    : launch_bwd_t<T, 2, HAS_OUT, HAS_CARRY>(a);
 }

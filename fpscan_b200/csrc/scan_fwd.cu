@@ -30,7 +30,7 @@ namespace fpscan {
 
 template <int NV>
 struct FwdCfg {
-  static constexpr int kStages = NV == 1 ? 4 : 3;
+  static constexpr int kStages = NV == 1 ? 4 : (NV == 2 ? 3 : 2);
   static constexpr int SV = kThreads * NV;  // 16-byte vectors per chunk
   static constexpr int smem_bytes() { return kStages * 2 * SV * 16; }
 };
@@ -125,10 +125,15 @@ __global__ void __launch_bounds__(kThreads, 4) scan_fwd_kernel(const FwdKParams 
     float a[E], b[E];
     if (valid) {
       Vec16<T> gv[NV], xv[NV];
+      {
+        uint4 rg[NV], rx[NV];
+        lds_vecs<NV>(&s_g[s][vi * NV], rg);
+        lds_vecs<NV>(&s_x[s][vi * NV], rx);
 #pragma unroll
-      for (int q = 0; q < NV; ++q) {
-        gv[q].raw = s_g[s][vi * NV + q];
-        xv[q].raw = s_x[s][vi * NV + q];
+        for (int q = 0; q < NV; ++q) {
+          gv[q].raw = rg[q];
+          xv[q].raw = rx[q];
+        }
       }
 #pragma unroll
       for (int i = 0; i < E; ++i) {
@@ -192,15 +197,12 @@ __global__ void __launch_bounds__(kThreads, 4) scan_fwd_kernel(const FwdKParams 
     for (int i = 0; i < E; ++i) yv[i] = skip_state ? b[i] : fmaf(a[i], state, b[i]);
 
     if (HAS_OUT && valid) {
-      Vec16<T> ov[NV];
+      float f[E];  // memory order
 #pragma unroll
-      for (int i = 0; i < E; ++i) {
-        const int j = REV ? E - 1 - i : i;
-        ov[j / V].e[j % V] = Elem<T>::store(yv[i]);
-      }
+      for (int i = 0; i < E; ++i) f[REV ? E - 1 - i : i] = yv[i];
       uint4* dst = reinterpret_cast<uint4*>(out + base + off) + vi * NV;
 #pragma unroll
-      for (int q = 0; q < NV; ++q) dst[q] = ov[q].raw;
+      for (int q = 0; q < NV; ++q) dst[q] = pack_vec<T>(f + q * V);
     }
 
     if (multi) {
@@ -261,6 +263,8 @@ static cudaError_t launch_fwd_t(const FwdArgs& a) {
 
 template <typename T, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
 static cudaError_t launch_fwd_nv(const FwdArgs& a) {
+  if constexpr (sizeof(T) == 4)
+    if (a.nv == 4) return launch_fwd_t<T, 4, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>(a);
   return a.nv == 1 ? launch_fwd_t<T, 1, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>(a)
                    : launch_fwd_t<T, 2, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>(a);
 }

@@ -369,3 +369,46 @@ def test_seq_shard_kernels_emulated(dtype, world, L):
 def test_device_status_clean():
     torch.cuda.synchronize()
     assert _lib.device_status(clear=True) == 0
+
+
+# ----------------------------------------------------------------- non-default kernel variants
+_VARIANT_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, {repo!r})
+import fpscan_b200 as fp, oracle
+errs = []
+for dtype in (torch.float32, torch.bfloat16):
+    for (b, d, L) in ((2, 5, 32), (3, 7, 1024), (2, 3, 8192), (1, 2, 65536)):
+        g = torch.Generator(device="cuda").manual_seed(L)
+        gates = (0.9 + 0.1 * torch.rand(b, d, L, generator=g, device="cuda")).to(dtype)
+        x = torch.randn(b, d, L, generator=g, device="cuda").to(dtype)
+        go = torch.randn(b, d, L, generator=g, device="cuda").to(dtype)
+        for rev in (False, True):
+            y = fp.scan_forward(gates, x, reverse=rev)
+            ref = oracle.scan_f64(gates.double().cpu().numpy(), x.double().cpu().numpy(), rev)
+            errs.append(oracle.normwise_error(y.double().cpu().numpy(), ref))
+        y = fp.scan_forward(gates, x)
+        dg, dt = fp.scan_backward(gates, y, go)
+        y64 = oracle.scan_f64(gates.double().cpu().numpy(), x.double().cpu().numpy())
+        dg64, dt64 = oracle.scan_bwd_f64(gates.double().cpu().numpy(), y64, go.double().cpu().numpy())
+        tol = 1e-5 if dtype == torch.float32 else 1e-2
+        e = max(oracle.normwise_error(dt.double().cpu().numpy(), dt64),
+                oracle.normwise_error(dg.double().cpu().numpy(), dg64))
+        assert e <= tol, (dtype, b, d, L, e)
+        assert max(errs) <= tol, (dtype, b, d, L, max(errs))
+print("ok")
+"""
+
+
+@pytest.mark.parametrize("nv", ["1", "2", "4"])
+def test_vector_width_variants(nv):
+    """FPSCAN_B200_NV selects the 1/2/4-vector kernel variants (read once per
+    process, so each runs in a child process)."""
+    import subprocess
+    import sys
+
+    repo = os.path.dirname(HERE)
+    env = dict(os.environ, FPSCAN_B200_NV=nv)
+    r = subprocess.run([sys.executable, "-c", _VARIANT_SCRIPT.format(repo=repo)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
