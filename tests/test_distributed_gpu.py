@@ -1,0 +1,98 @@
+"""Multi-GPU tests (NCCL, one process per GPU; skipped with fewer than 2
+GPUs): the sequence-sharded pscan (forward + backward through the real
+all-gather and the device carry kernels) and channel sharding, against the
+single-GPU result and the float64 oracle."""
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q, mode, dtype_name):
+    try:
+        import sys
+        sys.path.insert(0, REPO)
+        import torch.distributed as dist
+
+        import fpscan_b200 as fp
+        import oracle
+        from fpscan_b200.distributed import local_channels, seq_sharded_pscan
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, device_id=dev)
+        dtype = getattr(torch, dtype_name)
+        b, d, L = 2, 96, 8192 * world
+        gen = torch.Generator(device=dev).manual_seed(1234)  # same full tensors on every rank
+        g = (0.999 + 0.001 * torch.rand(b, d, L, generator=gen, device=dev)).to(dtype)
+        x = (torch.randn(b, d, L, generator=gen, device=dev) / L).to(dtype)
+        w = torch.randn(b, d, L, generator=gen, device=dev).to(dtype)
+        tol = 1e-5 if dtype == torch.float32 else 1e-2
+        if mode == "seq":
+            Lr = L // world
+            sl = slice(rank * Lr, (rank + 1) * Lr)
+            gl = g[..., sl].contiguous().requires_grad_()
+            xl = x[..., sl].contiguous().requires_grad_()
+            y = seq_sharded_pscan(gl, xl)
+            dgl, dxl = torch.autograd.grad(y, (gl, xl), w[..., sl].contiguous())
+            y64 = oracle.scan_f64(g.double().cpu().numpy(), x.double().cpu().numpy())
+            dg64, dt64 = oracle.scan_bwd_f64(g.double().cpu().numpy(), y64, w.double().cpu().numpy())
+            errs = [oracle.normwise_error(y.detach().double().cpu().numpy(), y64[..., sl]),
+                    oracle.normwise_error(dxl.double().cpu().numpy(), dt64[..., sl]),
+                    oracle.normwise_error(dgl.double().cpu().numpy(), dg64[..., sl])]
+        else:
+            gl, xl = local_channels(g, rank, world), local_channels(x, rank, world)
+            yl = fp.pscan(gl.contiguous(), xl.contiguous())
+            full = fp.scan_forward(g, x)
+            errs = [float((yl - local_channels(full, rank, world)).abs().max().item())]
+            tol = 0.0  # same kernel on the same rows: bit-identical
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, errs, tol, None))
+    except Exception:
+        q.put((rank, None, None, traceback.format_exc()))
+
+
+def _run(mode, dtype_name, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode, dtype_name))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+    for rank, errs, tol, tb in res:
+        assert tb is None, f"rank {rank}:\n{tb}"
+        assert max(errs) <= tol, (rank, errs)
+
+
+needs2 = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+
+
+@needs2
+@pytest.mark.parametrize("dtype_name", ["float32", "bfloat16"])
+def test_seq_sharded_nccl_matches_oracle(dtype_name):
+    _run("seq", dtype_name)
+
+
+@needs2
+def test_channel_sharded_nccl_bit_identical():
+    _run("chan", "bfloat16")
