@@ -43,6 +43,12 @@ CONFIGS = {
                          tokens_scale="0.1"),
     "halfbwd_fp16": dict(batch=8, dim=2048, seqlen=8192, dtype="float16", gates="sigmoid",
                          tokens_scale="0.1"),
+    # sequence-sharded fp32 fwd+bwd, seqlen split over the ranks
+    "shard_seq": dict(batch=4, dim=8192, seqlen=65536, dtype="float32", gates="0.999+0.001U",
+                      tokens_scale="1/L"),
+    # forward-only sweep, fp32, batch 2 x dim 256, seqlen 32..65536
+    "fwd_sweep": dict(batch=2, dim=256, seqlen=65536, dtype="float32", gates="0.99+0.01U",
+                      tokens_scale="1/L"),
 }
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the backward
@@ -414,6 +420,141 @@ def _e2e(args, cfg, gates_d, tokens_d, grad_out_d, device, world):
             "path": "pinned host -> fpscan_b200.pscan fwd+bwd -> pinned host, one stream"}
 
 
+def _timed_loop(step, steps, stream, world):
+    """Barrier + sync, K steps bracketed by CUDA events, max over ranks (ms)."""
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=stream.device)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_shard_seq(args, cfg):
+    """every rank holds positions [r*L/N, (r+1)*L/N) of all
+    4 x 8192 rows (fp32); one step = seq_sharded_pscan forward + backward
+    (reduce, NCCL all-gather of the per-row carries, combine, scan -- both
+    directions).  Credited bytes: 8*N*s of the whole sequence."""
+    import torch.distributed as dist
+
+    import fpscan_b200
+    from fpscan_b200 import _lib
+    from fpscan_b200.distributed import seq_sharded_pscan
+
+    world, rank, local = _dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    _lib.load()
+    B, D, L = cfg["batch"], cfg["dim"], cfg["seqlen"]
+    Lr = L // world
+    gen = torch.Generator(device=device).manual_seed(5 + rank)
+    g = (0.999 + 0.001 * torch.rand(B, D, Lr, generator=gen, device=device)).requires_grad_()
+    x = (torch.randn(B, D, Lr, generator=gen, device=device) / L).requires_grad_()
+    go = torch.randn(B, D, Lr, generator=gen, device=device)
+
+    def step():
+        if world > 1:
+            y = seq_sharded_pscan(g, x)
+        else:
+            y = fpscan_b200.pscan(g, x)
+        torch.autograd.grad(y, (g, x), go)
+
+    for _ in range(args.warmup):
+        step()
+    stream = torch.cuda.current_stream(device)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    ms = _timed_loop(step, args.steps, stream, world)
+    clock_info = clocks.stop() if clocks else None
+    s = 4
+    value = 8 * B * D * L * s * args.steps / (ms / 1e3) / 1e9
+    peak, peak_kind = _peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "float32", "data": "synthetic (seeded; BASELINE config 5 distributions)",
+            "config": {"workload": f"shard_seq: pscan fwd+bwd fp32 batch={B} dim={D} seqlen={L}, "
+                                   f"seqlen split over {world} GPU(s)",
+                       "batch": B, "dim": D, "seqlen": L, "parallelism": f"seq-shard x{world}",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "pct_of_hbm_peak": round(100 * value / world / peak, 2), "peak_source": peak_kind,
+            "gpu_launches": (6 if world > 1 else 2) * args.steps,
+            "clocks": clock_info, "device_status": _lib.device_status()}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_fwd_sweep(args, cfg):
+    """BASELINE config 2 on one GPU: scan_forward (reverse False and True),
+    fp32, 2 x 256 channels, every seqlen 32..65536; p50 of per-call CUDA
+    events with L2 flushed (a 512 MiB write) before every call.  `value` is
+    the forward GB/s at seqlen 65536; the table has every row."""
+    import fpscan_b200
+    from fpscan_b200 import _lib
+
+    world, rank, local = _dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    _lib.load()
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=device)
+    table = []
+    B, D = cfg["batch"], cfg["dim"]
+    for lg in range(5, 17):
+        L = 1 << lg
+        gen = torch.Generator(device=device).manual_seed(L)
+        g = 0.99 + 0.01 * torch.rand(B, D, L, generator=gen, device=device)
+        x = torch.randn(B, D, L, generator=gen, device=device) / L
+        out = torch.empty_like(x)
+        row = {"seqlen": L}
+        for rev in (False, True):
+            for _ in range(args.warmup):
+                fpscan_b200.scan_forward(g, x, rev, out)
+            ts = []
+            for _ in range(max(args.steps, 20)):
+                flush.zero_()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record()
+                fpscan_b200.scan_forward(g, x, rev, out)
+                b.record()
+                torch.cuda.synchronize()
+                ts.append(a.elapsed_time(b))
+            p50 = statistics.median(ts)
+            key = "reverse" if rev else "forward"
+            row[f"{key}_p50_ms"] = round(p50, 5)
+            row[f"{key}_gbs"] = round(3 * x.numel() * 4 / (p50 / 1e3) / 1e9, 1)
+        table.append(row)
+    peak, peak_kind = _peaks()
+    last = table[-1]
+    print(json.dumps({
+        "metric": METRIC, "value": last["forward_gbs"], "unit": "GB/s", "n_gpus": 1,
+        "steps": max(args.steps, 20), "warmup": args.warmup,
+        "ms_per_step": last["forward_p50_ms"], "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "float32", "data": "synthetic (seeded; BASELINE config 2)",
+        "config": {"workload": "fwd_sweep: scan_forward fp32 batch=2 dim=256 seqlen=32..65536",
+                   "batch": B, "dim": D, "l2": "flushed before every call (512 MiB write)"},
+        "pct_of_hbm_peak": round(100 * last["forward_gbs"] / peak, 2), "peak_source": peak_kind,
+        "sweep": table}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -429,6 +570,10 @@ def main():
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif args.config == "shard_seq":
+        run_shard_seq(args, cfg)
+    elif args.config == "fwd_sweep":
+        run_fwd_sweep(args, cfg)
     else:
         run_fpscan(args, cfg)
 
