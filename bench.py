@@ -92,7 +92,7 @@ class ClockSampler:
         except Exception:
             pass
         self.cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                    "-lms", "200"] + ([f"--id={bus}"] if bus else [])
+                    "-lms", "50"] + ([f"--id={bus}"] if bus else [])
 
     def start(self):
         try:
@@ -371,29 +371,22 @@ def run_fpscan(args, cfg):
 
 
 def _e2e(args, cfg, gates_d, tokens_d, grad_out_d, device, world):
-    """Same metric through the public API with host (pinned) buffers: every
-    step copies this step's inputs host->device and all results back."""
+    """Same metric through the public host-memory API
+    (fpscan_b200.offload.scan_fwd_bwd_host): every step copies this step's
+    inputs from pinned host memory to the device and all three results
+    (y, grad_gates, grad_tokens) back, pipelined over row blocks."""
     import torch.distributed as dist
 
-    import fpscan_b200
+    from fpscan_b200.offload import scan_fwd_bwd_host
 
     g_h = gates_d.cpu().pin_memory()
     x_h = tokens_d.cpu().pin_memory()
     go_h = grad_out_d.cpu().pin_memory()
-    y_h = torch.empty_like(g_h).pin_memory()
-    dg_h = torch.empty_like(g_h).pin_memory()
-    dt_h = torch.empty_like(g_h).pin_memory()
+    outs = [torch.empty_like(g_h).pin_memory() for _ in range(3)]
     stream = torch.cuda.current_stream(device)
 
     def step():
-        g = g_h.to(device, non_blocking=True).requires_grad_()
-        x = x_h.to(device, non_blocking=True).requires_grad_()
-        go = go_h.to(device, non_blocking=True)
-        y = fpscan_b200.pscan(g, x)
-        dg, dt = torch.autograd.grad(y, (g, x), go)
-        y_h.copy_(y.detach(), non_blocking=True)
-        dg_h.copy_(dg, non_blocking=True)
-        dt_h.copy_(dt, non_blocking=True)
+        scan_fwd_bwd_host(g_h, x_h, go_h, *outs, device=device)
 
     step()
     torch.cuda.synchronize()
@@ -417,7 +410,8 @@ def _e2e(args, cfg, gates_d, tokens_d, grad_out_d, device, world):
     nbytes = g_h.numel() * s
     return {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 3 * nbytes,
             "d2h_bytes_per_step": 3 * nbytes, "steps": k,
-            "path": "pinned host -> fpscan_b200.pscan fwd+bwd -> pinned host, one stream"}
+            "path": "pinned host -> fpscan_b200.offload.scan_fwd_bwd_host (row blocks, "
+                    "3 streams: H2D / kernels / D2H overlapped) -> pinned host"}
 
 
 def _timed_loop(step, steps, stream, world):
@@ -558,7 +552,7 @@ def run_fwd_sweep(args, cfg):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["fpscan", "reference"], default="fpscan")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="shard_bd")
