@@ -17,10 +17,13 @@ _c_i64 = ctypes.c_int64
 _c_int = ctypes.c_int
 _vp = ctypes.c_void_p
 
-# name -> argtypes, every function returns int except fpscan_last_error.
+# name -> argtypes; every function returns int except fpscan_last_error
+# (const char*) and fpscan_scan_fwd_workspace_bytes (int64).
 SIGNATURES = {
     "fpscan_abi_version": [],
     "fpscan_scan_fwd": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
+    "fpscan_scan_fwd_workspace_bytes": [_c_i64, _c_i64, _c_i64, _c_int],
+    "fpscan_scan_fwd_ws": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp, _c_i64, _vp],
     "fpscan_scan_bwd": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_fwd_reduce": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_fwd_scan": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
@@ -57,7 +60,8 @@ def load() -> ctypes.CDLL:
         for name, argtypes in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = argtypes
-            fn.restype = ctypes.c_char_p if name == "fpscan_last_error" else ctypes.c_int
+            fn.restype = {"fpscan_last_error": ctypes.c_char_p,
+                          "fpscan_scan_fwd_workspace_bytes": ctypes.c_int64}.get(name, ctypes.c_int)
         ver = lib.fpscan_abi_version()
         if ver != EXPECTED_ABI_VERSION:
             raise ImportError(f"libfpscan_b200 ABI version {ver}, expected {EXPECTED_ABI_VERSION}")

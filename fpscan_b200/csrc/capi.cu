@@ -162,6 +162,46 @@ int fpscan_scan_fwd(const void* gates, const void* tokens, void* out, int64_t ba
   return cuda_result(launch_fwd(a), "fpscan_scan_fwd launch");
 }
 
+int64_t fpscan_scan_fwd_workspace_bytes(int64_t batch, int64_t dim, int64_t seqlen, int dtype) {
+  int64_t rows = 0;
+  if (check_dtype(dtype) != FPSCAN_OK) return 0;
+  if (check_shape(batch, dim, seqlen, kRefMinL, kRefMaxL, &rows) != FPSCAN_OK) return 0;
+  const int p = split_segments(rows, seqlen, dtype, split_slots(dtype, num_sms_current()));
+  return split_workspace_bytes(rows, p);
+}
+
+int fpscan_scan_fwd_ws(const void* gates, const void* tokens, void* out, int64_t batch,
+                       int64_t dim, int64_t seqlen, int dtype, int reverse, void* workspace,
+                       int64_t workspace_bytes, void* stream) {
+  int64_t rows = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape(batch, dim, seqlen, kRefMinL, kRefMaxL, &rows));
+  if (rows == 0) return ok();
+  const int p = split_segments(rows, seqlen, dtype, split_slots(dtype, num_sms_current()));
+  if (p <= 1) return fpscan_scan_fwd(gates, tokens, out, batch, dim, seqlen, dtype, reverse, stream);
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(tokens, "tokens"));
+  FPSCAN_TRY(check_ptr(out, "out"));
+  FPSCAN_TRY(check_ptr(workspace, "workspace"));
+  const int64_t need = split_workspace_bytes(rows, p);
+  if (workspace_bytes < need)
+    return fail(FPSCAN_ERR_INVALID, "workspace too small: %lld bytes, need %lld",
+                (long long)workspace_bytes, (long long)need);
+  const uintptr_t bytes = (uintptr_t)(rows * seqlen * dtype_size(dtype));
+  const Span so{"out", (uintptr_t)out, (uintptr_t)out + bytes};
+  const Span sg{"gates", (uintptr_t)gates, (uintptr_t)gates + bytes};
+  const Span st{"tokens", (uintptr_t)tokens, (uintptr_t)tokens + bytes};
+  const Span sw{"workspace", (uintptr_t)workspace, (uintptr_t)workspace + (uintptr_t)need};
+  for (const Span* in : {&sg, &st})
+    if (overlaps(so, *in) && so.lo != in->lo)
+      return fail(FPSCAN_ERR_INVALID, "out partially overlaps %s", in->name);
+  for (const Span* in : {&sg, &st, &so})
+    if (overlaps(sw, *in)) return fail(FPSCAN_ERR_INVALID, "workspace overlaps %s", in->name);
+  SplitArgs a{gates, tokens, out, workspace, rows, seqlen, p, dtype, reverse ? 1 : 0,
+              static_cast<cudaStream_t>(stream)};
+  return cuda_result(launch_split(a), "fpscan_scan_fwd_ws launch");
+}
+
 int fpscan_scan_bwd(const void* gates, const void* y, const void* grad_out, void* dgates,
                     void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
                     void* stream) {

@@ -50,7 +50,24 @@ struct BwdArgs {
   int nv = 2;           // 16-byte vectors per thread per chunk (1 or 2)
 };
 
+struct SplitArgs {
+  const void* gates;
+  const void* tokens;
+  void* out;
+  void* workspace;      // >= split_workspace_bytes(rows, segments), 16-byte aligned
+  int64_t rows;
+  int64_t seqlen;
+  int64_t segments;     // per row, power of two (split_segments)
+  int dtype;
+  int reverse;
+  cudaStream_t stream;
+};
+
 cudaError_t launch_fwd(const FwdArgs& a);
+cudaError_t launch_split(const SplitArgs& a);
+int split_slots(int dtype, int num_sms);
+int split_segments(int64_t rows, int64_t seqlen, int dtype, int slots);
+int64_t split_workspace_bytes(int64_t rows, int segments);
 cudaError_t launch_bwd(const BwdArgs& a);
 cudaError_t launch_carry_combine(const float* gathered, int world, int rank, int64_t rows,
                                  int reverse, float* out, cudaStream_t stream);

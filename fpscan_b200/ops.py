@@ -76,16 +76,42 @@ def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+# Split-row workspaces, one per (device, stream): calls ordered on one stream
+# may share one; it is zeroed once when (re)allocated.
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    key = (device.index, stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
 def fullscan_forward(gates: torch.Tensor, tokens: torch.Tensor, out: torch.Tensor,
                      reverse: bool) -> torch.Tensor:
     """Same contract as the reference extension's ``fullscan_forward``
-    (csrc/main.cpp:10 -> warpscan_fwd): validates, scans into ``out``, returns it."""
+    (csrc/main.cpp:10 -> warpscan_fwd): validates, scans into ``out``, returns it.
+    Few-channel, long-sequence shapes go to the split-row kernel, which needs
+    a small per-stream workspace (kept here)."""
     validate(gates, tokens, out)
     b, d, l = tokens.shape
+    lib = _lib.load()
+    code = DTYPE_CODES[tokens.dtype]
     with torch.cuda.device(tokens.device):
-        _lib.call("fpscan_scan_fwd", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
-                  b, d, l, DTYPE_CODES[tokens.dtype], 1 if reverse else 0,
-                  _stream_ptr(tokens.device))
+        stream = _stream_ptr(tokens.device)
+        ws_bytes = lib.fpscan_scan_fwd_workspace_bytes(b, d, l, code)
+        if ws_bytes > 0:
+            ws = _workspace(tokens.device, stream, ws_bytes)
+            _lib.check(lib.fpscan_scan_fwd_ws(gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
+                                              b, d, l, code, 1 if reverse else 0, ws.data_ptr(),
+                                              ws.numel(), stream), "fpscan_scan_fwd_ws")
+        else:
+            _lib.check(lib.fpscan_scan_fwd(gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
+                                           b, d, l, code, 1 if reverse else 0, stream),
+                       "fpscan_scan_fwd")
     return out
 
 

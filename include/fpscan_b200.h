@@ -58,6 +58,31 @@ FPSCAN_API int fpscan_scan_fwd(const void* gates, const void* tokens, void* out,
                     int64_t dim, int64_t seqlen, int dtype, int reverse, void* stream);
 
 /*
+ * Bytes of workspace fpscan_scan_fwd_ws needs for this shape (0: none; the
+ * shape is then served by the fpscan_scan_fwd kernel).  Non-zero when
+ * batch*dim is too small to fill the GPU with one CTA per row, so rows are
+ * split across CTAs.  Depends on the current device (its SM count).
+ * No reference counterpart (the reference runs one CTA per row,
+ * csrc/full_scan/full_scan.cu:190).
+ */
+FPSCAN_API int64_t fpscan_scan_fwd_workspace_bytes(int64_t batch, int64_t dim, int64_t seqlen,
+                                                   int dtype);
+
+/*
+ * fpscan_scan_fwd with a caller-provided device workspace (16-byte aligned,
+ * at least fpscan_scan_fwd_workspace_bytes; may be NULL when that is 0).
+ * Zero the workspace once after allocating it; afterwards it can be reused by
+ * any number of calls that are ordered on the GPU (e.g. one stream).
+ * Calls that overlap on the GPU must use different workspaces.
+ * Same results and contract as fpscan_scan_fwd (which it replaces for
+ * few-channel, long-sequence shapes).
+ */
+FPSCAN_API int fpscan_scan_fwd_ws(const void* gates, const void* tokens, void* out,
+                                  int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                                  int reverse, void* workspace, int64_t workspace_bytes,
+                                  void* stream);
+
+/*
  * Fused backward of y = scan(gates, tokens):
  *   dtokens[t] = gates[t+1]*dtokens[t+1] + grad_out[t]  (last element: grad_out)
  *   dgates[t]  = dtokens[t] * y[t-1]                      (first element: 0*dtokens)
@@ -108,8 +133,9 @@ FPSCAN_API int fpscan_carry_combine(const float* gathered, int world, int rank, 
 FPSCAN_API const char* fpscan_last_error(void);
 
 /* Synchronously read (and if `clear`, reset) the current device's status
- * word.  Bit 0: a kernel gave up a bounded wait (results of that launch are
- * not valid).  0 = healthy. */
+ * word.  Bit 0: a kernel gave up a bounded wait on its own copies; bit 1: a
+ * split-row scan gave up waiting for a preceding segment.  Results of such a
+ * launch are not valid.  0 = healthy. */
 FPSCAN_API int fpscan_device_status(unsigned* status, int clear);
 
 #ifdef __cplusplus

@@ -1,5 +1,6 @@
 """Host-memory pipelined forward+backward (fpscan_b200.offload) against the
-device-resident path: same kernels on the same rows, so bit-identical."""
+device-resident path (the same kernels; few-row device calls may take the
+split-row forward, so the comparison is within the normwise tolerance)."""
 import pytest
 import torch
 
@@ -23,9 +24,11 @@ def test_offload_matches_device_path(dtype, shape, block_bytes, depth):
     gd, xd, god = g.cuda(), x.cuda(), go.cuda()
     yd = fp.scan_forward(gd, xd)
     dgd, dtd = fp.scan_backward(gd, yd, god)
-    assert torch.equal(y, yd.cpu())
-    assert torch.equal(dt, dtd.cpu())
-    assert torch.equal(dg, dgd.cpu())
+    import oracle
+
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    for a, b in ((y, yd), (dt, dtd), (dg, dgd)):
+        assert oracle.normwise_error(a.double().numpy(), b.double().cpu().numpy()) <= tol
 
 
 def test_offload_rejects_device_tensors():

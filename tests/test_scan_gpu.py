@@ -412,3 +412,50 @@ def test_vector_width_variants(nv):
     r = subprocess.run([sys.executable, "-c", _VARIANT_SCRIPT.format(repo=repo)], env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+# ----------------------------------------------------------------- split-row (few rows, long L) path
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("batch,dim,seqlen", [(2, 256, 65536), (1, 1, 65536), (2, 3, 8192),
+                                              (1, 7, 16384), (2, 256, 4096)])
+def test_split_row_path_vs_one_cta_per_row(dtype, batch, dim, seqlen):
+    """fpscan_scan_fwd_ws (rows split across CTAs, decoupled look-back) against
+    fpscan_scan_fwd (one CTA per row) and the oracle, three calls in a row on
+    the same workspace (epoch-tagged status words are reused)."""
+    lib = _lib.load()
+    code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[dtype]
+    gates, tokens = _make_inputs(batch, dim, seqlen, dtype, seed=seqlen + dim)
+    ws_bytes = lib.fpscan_scan_fwd_workspace_bytes(batch, dim, seqlen, code)
+    ws = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=DEVICE)
+    stream = torch.cuda.current_stream().cuda_stream
+    for rev in (False, True):
+        ref = oracle.scan_f64(_np64(gates), _np64(tokens), reverse=rev)
+        plain = torch.empty_like(tokens)
+        _lib.check(lib.fpscan_scan_fwd(gates.data_ptr(), tokens.data_ptr(), plain.data_ptr(), batch,
+                                       dim, seqlen, code, int(rev), stream), "fwd")
+        for _ in range(3):
+            out = torch.full_like(tokens, float("nan"))
+            _lib.check(lib.fpscan_scan_fwd_ws(gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
+                                              batch, dim, seqlen, code, int(rev), ws.data_ptr(),
+                                              ws.numel(), stream), "fwd_ws")
+            _check(out, ref, dtype, f"split rev={rev}")
+            assert oracle.normwise_error(_np64(out), _np64(plain)) <= NORM_TOL[dtype]
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
+
+
+def test_split_row_workspace_checks():
+    lib = _lib.load()
+    gates, tokens = _make_inputs(2, 4, 65536, torch.float32)
+    need = lib.fpscan_scan_fwd_workspace_bytes(2, 4, 65536, 0)
+    assert need > 0
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEVICE)
+    out = torch.empty_like(tokens)
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.fpscan_scan_fwd_ws(gates.data_ptr(), tokens.data_ptr(), out.data_ptr(), 2, 4, 65536,
+                                  0, 0, ws.data_ptr(), need - 16, s) == 1
+    assert b"workspace" in lib.fpscan_last_error()
+    assert lib.fpscan_scan_fwd_ws(gates.data_ptr(), tokens.data_ptr(), out.data_ptr(), 2, 4, 65536,
+                                  0, 0, 0, 0, s) == 1
+    # many rows: no workspace needed, plain kernel
+    assert lib.fpscan_scan_fwd_workspace_bytes(64, 1024, 4096, 0) == 0
