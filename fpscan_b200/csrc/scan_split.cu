@@ -1,8 +1,7 @@
 // Split-row forward / reverse scan for few, long rows, sm_100a.
 //
-// When batch*dim is smaller than the number of CTA slots of the GPU (e.g.
-// 512 rows), one CTA per row leaves SMs idle and keeps
-// too few bytes in flight.  Here every row is cut into segments of 4 chunks
+// When batch*dim is far smaller than the number of CTA slots of the GPU,
+// one CTA per row leaves SMs idle and keeps too few bytes in flight.  Here every row is cut into segments of 4 chunks
 // (32 KiB per tensor) and each segment is one tile, taken in order from an
 // atomic tile counter (so every tile's predecessors are already running):
 //   stage   the whole segment (gates and tokens, 64 KiB) with non-multicast
@@ -242,14 +241,19 @@ __global__ void __launch_bounds__(kThreads, 3) scan_split_kernel(const SplitKPar
   }
 }
 
-// Segments per row for the split path (1 = not used): segments are fixed at
-// kSegChunks chunks (32 KiB per tensor); split only when the rows alone
-// cannot fill the GPU's CTA slots and a row holds at least two segments.
+// Segments per row for the split path (1 = not used).  Segments are fixed
+// at kSegChunks chunks (32 KiB per tensor).  Measured on B200 (fp32 and
+// bf16, L = 16K..64K): splitting wins only when rows are few and long --
+// 8 rows: +66%, 64 rows x 64K fp32: +6% -- and loses once the tiles exceed
+// about two waves or a row has fewer than 4 segments, so it is used only
+// when rows * segments <= 2 * slots and segments >= 4.
 int split_segments(int64_t rows, int64_t seqlen, int dtype, int slots) {
   const int es = dtype_size(dtype);
   const int64_t seg = (int64_t)kSegChunks * kThreads * kSplitNV * (16 / es);
-  if (rows <= 0 || rows >= slots || seqlen < 2 * seg) return 1;
-  return (int)(seqlen / seg);
+  if (rows <= 0 || seqlen < 4 * seg) return 1;
+  const int64_t p = seqlen / seg;
+  if (rows * p > 2 * (int64_t)slots) return 1;
+  return (int)p;
 }
 
 int split_slots(int dtype, int num_sms) {

@@ -416,8 +416,9 @@ def test_vector_width_variants(nv):
 
 # ----------------------------------------------------------------- split-row (few rows, long L) path
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("batch,dim,seqlen", [(2, 256, 65536), (1, 1, 65536), (2, 3, 8192),
-                                              (1, 7, 16384), (2, 256, 4096)])
+@pytest.mark.parametrize("batch,dim,seqlen", [(2, 256, 65536), (1, 1, 65536), (1, 8, 65536),
+                                              (2, 16, 32768), (1, 7, 65536), (1, 64, 65536),
+                                              (2, 3, 8192)])
 def test_split_row_path_vs_one_cta_per_row(dtype, batch, dim, seqlen):
     """fpscan_scan_fwd_ws (rows split across CTAs, decoupled look-back) against
     fpscan_scan_fwd (one CTA per row) and the oracle, three calls in a row on
