@@ -130,6 +130,17 @@ constexpr int64_t kShardMaxL = int64_t(1) << 24;
   } while (0)
 
 }  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
 }  // namespace fpscan
 
 using namespace fpscan;

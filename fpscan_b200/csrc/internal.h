@@ -63,6 +63,9 @@ struct SplitArgs {
   cudaStream_t stream;
 };
 
+// Records `fmt` as this thread's fpscan_last_error() message; returns code.
+int set_error(int code, const char* fmt, ...);
+
 cudaError_t launch_fwd(const FwdArgs& a);
 cudaError_t launch_split(const SplitArgs& a);
 int split_slots(int dtype, int num_sms);

@@ -83,6 +83,23 @@ FPSCAN_API int fpscan_scan_fwd_ws(const void* gates, const void* tokens, void* o
                                   void* stream);
 
 /*
+ * fpscan_scan_fwd for callers that cannot allocate device memory (a host
+ * that owns every GPU allocation, a service that forbids cudaMalloc/cudaFree
+ * while running, C code without a caching allocator).  Same arguments and
+ * results as fpscan_scan_fwd / fpscan_scan_fwd_ws; the scratch that
+ * few-channel, long-sequence shapes need comes from a fixed array inside the
+ * library (8,448 bytes per GPU, held until exit: at most 512 split
+ * segments; larger needs are rejected with FPSCAN_ERR_INVALID).  The first
+ * call on a device looks the array up and clears it (make it before any
+ * stream capture).  Calls share the array: calls that overlap on the GPU
+ * race and must not be issued.  Allocates nothing.
+ * No counterpart in the reference.
+ */
+FPSCAN_API int fpscan_scan_fwd_noalloc(const void* gates, const void* tokens, void* out,
+                                       int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                                       int reverse, void* stream);
+
+/*
  * Fused backward of y = scan(gates, tokens):
  *   dtokens[t] = gates[t+1]*dtokens[t+1] + grad_out[t]  (last element: grad_out)
  *   dgates[t]  = dtokens[t] * y[t-1]                      (first element: 0*dtokens)
