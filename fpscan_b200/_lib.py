@@ -25,6 +25,7 @@ SIGNATURES = {
     "fpscan_scan_fwd_workspace_bytes": [_c_i64, _c_i64, _c_i64, _c_int],
     "fpscan_scan_fwd_ws": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp, _c_i64, _vp],
     "fpscan_scan_fwd_noalloc": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
+    "fpscan_scan_fwd_init": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
     "fpscan_scan_bwd": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_fwd_reduce": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_fwd_scan": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],

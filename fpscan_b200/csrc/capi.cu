@@ -242,6 +242,30 @@ int fpscan_scan_bwd(const void* gates, const void* y, const void* grad_out, void
   return cuda_result(launch_bwd(a), "fpscan_scan_bwd launch");
 }
 
+int fpscan_scan_fwd_init(const void* gates, const void* tokens, void* out, const float* init,
+                         int64_t batch, int64_t dim, int64_t seqlen, int dtype, int reverse,
+                         void* stream) {
+  int64_t rows = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape(batch, dim, seqlen, kRefMinL, kRefMaxL, &rows));
+  if (rows == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(tokens, "tokens"));
+  FPSCAN_TRY(check_ptr(out, "out"));
+  if (!init) return fail(FPSCAN_ERR_INVALID, "init is NULL");
+  const uintptr_t bytes = (uintptr_t)(rows * seqlen * dtype_size(dtype));
+  const Span so{"out", (uintptr_t)out, (uintptr_t)out + bytes};
+  const Span sg{"gates", (uintptr_t)gates, (uintptr_t)gates + bytes};
+  const Span st{"tokens", (uintptr_t)tokens, (uintptr_t)tokens + bytes};
+  for (const Span* in : {&sg, &st})
+    if (overlaps(so, *in) && so.lo != in->lo)
+      return fail(FPSCAN_ERR_INVALID, "out partially overlaps %s", in->name);
+  FwdArgs a{gates, tokens, out, init, nullptr, nullptr, rows, seqlen, dtype, reverse ? 1 : 0,
+            num_sms_current(), static_cast<cudaStream_t>(stream)};
+  a.nv = tuned_nv(true, dtype);
+  return cuda_result(launch_fwd(a), "fpscan_scan_fwd_init launch");
+}
+
 int fpscan_shard_fwd_reduce(const void* gates, const void* tokens, float* carry_a,
                             float* carry_b, int64_t rows, int64_t seqlen, int dtype,
                             void* stream) {

@@ -279,8 +279,10 @@ static cudaError_t launch_fwd_dtype(const FwdArgs& a) {
   if (has_out && !has_init && !has_co)
     return a.reverse ? launch_fwd_nv<T, true, true, false, false>(a)
                      : launch_fwd_nv<T, false, true, false, false>(a);
+  if (has_out && has_init && !has_co)
+    return a.reverse ? launch_fwd_nv<T, true, true, true, false>(a)
+                     : launch_fwd_nv<T, false, true, true, false>(a);
   if (a.reverse) return cudaErrorInvalidValue;
-  if (has_out && has_init && !has_co) return launch_fwd_nv<T, false, true, true, false>(a);
   if (has_out && has_init && has_co) return launch_fwd_nv<T, false, true, true, true>(a);
   if (has_out && !has_init && has_co) return launch_fwd_nv<T, false, true, false, true>(a);
   if (!has_out && !has_init && has_co) return launch_fwd_nv<T, false, false, false, true>(a);

@@ -115,17 +115,41 @@ def fullscan_forward(gates: torch.Tensor, tokens: torch.Tensor, out: torch.Tenso
     return out
 
 
+def _check_state(state: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
+    if state.shape != tokens.shape[:2]:
+        raise RuntimeError(f"initial_state must have shape {tuple(tokens.shape[:2])} "
+                           f"(batch, dim), got {tuple(state.shape)}")
+    if state.device != tokens.device:
+        raise RuntimeError("initial_state must be on the device of tokens")
+    return state.to(torch.float32).contiguous()
+
+
 def scan_forward(gates: torch.Tensor, tokens: torch.Tensor, reverse: bool = False,
-                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 out: Optional[torch.Tensor] = None,
+                 initial_state: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Linear-recurrence scan y[t] = gates[t]*y[t-1] + tokens[t] (no autograd).
 
     ``reverse=True`` scans from the end: y[t] = gates[t]*y[t+1] + tokens[t].
     ``out`` (optional) receives the result and is returned.
+    ``initial_state`` (optional, shape (batch, dim)) replaces the zero state
+    entering the first element in scan order (then that element's gate is
+    used: y[0] = gates[0]*initial_state + tokens[0]).  The final state is
+    the last element of the result in scan order.  The reference has only
+    the zero state.
     """
     _lib.load()  # fail loudly before allocating if the library is missing
     if out is None:
         out = torch.empty_like(tokens)
-    return fullscan_forward(gates, tokens, out, reverse)
+    if initial_state is None:
+        return fullscan_forward(gates, tokens, out, reverse)
+    validate(gates, tokens, out)
+    h0 = _check_state(initial_state, tokens)
+    b, d, l = tokens.shape
+    with torch.cuda.device(tokens.device):
+        _lib.call("fpscan_scan_fwd_init", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
+                  h0.data_ptr(), b, d, l, DTYPE_CODES[tokens.dtype], 1 if reverse else 0,
+                  _stream_ptr(tokens.device))
+    return out
 
 
 def scan_backward(gates: torch.Tensor, y: torch.Tensor, grad_output: torch.Tensor):
@@ -161,6 +185,41 @@ class PScan(torch.autograd.Function):
         return scan_backward(gates, out, grad_output)
 
 
-def pscan(gates: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
-    """Differentiable scan (fpscan/ops.py:86-87)."""
-    return PScan.apply(gates, tokens)
+class PScanWithState(torch.autograd.Function):
+    """Differentiable scan with an initial state h0 (batch, dim):
+    y[0] = gates[0]*h0 + tokens[0].  Gradients: the fused backward with h0
+    as y[-1] gives grad_gates and grad_tokens; grad_h0 = gates[0]*grad_tokens[0]."""
+
+    @staticmethod
+    def forward(ctx, gates, tokens, h0):
+        out = scan_forward(gates, tokens, initial_state=h0)
+        h0f = _check_state(h0, tokens)
+        ctx.save_for_backward(gates, out, h0f)
+        ctx.h0_dtype = h0.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        gates, out, h0f = ctx.saved_tensors
+        grad_output = grad_output.contiguous()
+        validate(gates, grad_output)
+        b, d, l = grad_output.shape
+        dgates = torch.empty_like(grad_output)
+        dtokens = torch.empty_like(grad_output)
+        zero = torch.zeros_like(h0f)
+        with torch.cuda.device(grad_output.device):
+            _lib.call("fpscan_shard_bwd_scan", gates.data_ptr(), out.data_ptr(),
+                      grad_output.data_ptr(), dgates.data_ptr(), dtokens.data_ptr(),
+                      zero.data_ptr(), h0f.data_ptr(), b * d, l,
+                      DTYPE_CODES[grad_output.dtype], _stream_ptr(grad_output.device))
+        dh0 = (gates[..., 0].float() * dtokens[..., 0].float()).to(ctx.h0_dtype)
+        return dgates, dtokens, dh0
+
+
+def pscan(gates: torch.Tensor, tokens: torch.Tensor,
+          initial_state: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Differentiable scan (fpscan/ops.py:86-87); ``initial_state`` (batch,
+    dim), optional and differentiable, replaces the zero initial state."""
+    if initial_state is None:
+        return PScan.apply(gates, tokens)
+    return PScanWithState.apply(gates, tokens, initial_state)

@@ -83,6 +83,17 @@ FPSCAN_API int fpscan_scan_fwd_ws(const void* gates, const void* tokens, void* o
                                   void* stream);
 
 /*
+ * Scan with a per-row initial state `init` (fp32, batch*dim values):
+ * y[0] = gates[0]*init + tokens[0] (reverse: y[L-1] = gates[L-1]*init +
+ * tokens[L-1]).  The final state is the last element of out in scan order.
+ * Otherwise as fpscan_scan_fwd.  Extends the reference, whose initial state
+ * is fixed at zero (csrc/full_scan/full_scan.cu:96).
+ */
+FPSCAN_API int fpscan_scan_fwd_init(const void* gates, const void* tokens, void* out,
+                                    const float* init, int64_t batch, int64_t dim,
+                                    int64_t seqlen, int dtype, int reverse, void* stream);
+
+/*
  * fpscan_scan_fwd for callers that cannot allocate device memory (a host
  * that owns every GPU allocation, a service that forbids cudaMalloc/cudaFree
  * while running, C code without a caching allocator).  Same arguments and
