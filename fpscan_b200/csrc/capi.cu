@@ -105,9 +105,9 @@ int cuda_result(cudaError_t e, const char* what) {
 // Vectors per thread per chunk.  2 (default) amortises the per-chunk scan and
 // barrier over twice the data; FPSCAN_B200_NV=1 / =4 select the one- and
 // (fp32 only) four-vector variants (a tuning knob read once per process).
-// Measured defaults on B200 (config 4, 1.3 G elements): the forward scan of
-// half types is fastest with 1 vector per thread (more resident CTAs), every
-// other case with 2.
+// Measured defaults on B200 (configs 4 and 5): the forward scan is fastest
+// with 1 vector per thread (more resident CTAs / a deeper ring), the fused
+// backward with 2.
 int tuned_nv(bool forward, int dtype) {
   static const int env = [] {
     const char* v = getenv("FPSCAN_B200_NV");
@@ -117,7 +117,7 @@ int tuned_nv(bool forward, int dtype) {
     return 0;
   }();
   if (env) return env;
-  return (forward && dtype != kF32) ? 1 : 2;
+  return forward ? 1 : 2;
 }
 
 constexpr int64_t kRefMinL = 32, kRefMaxL = 65536;  // csrc/full_scan/full_scan.cu:207-233

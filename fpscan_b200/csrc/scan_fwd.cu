@@ -28,9 +28,15 @@
 
 namespace fpscan {
 
-template <int NV>
+// Pipeline depth and resident-CTA target, measured on B200 (forward, config
+// 4 / config 5 sizes): fp32 with one vector per thread is fastest with an
+// 8-deep ring at 3 CTAs/SM; half types with one vector per thread with 4
+// stages at 4 CTAs/SM; two vectors per thread with 3 stages.
+template <typename T, int NV>
 struct FwdCfg {
-  static constexpr int kStages = NV == 1 ? 4 : (NV == 2 ? 3 : 2);
+  static constexpr bool kDeep = sizeof(T) == 4 && NV == 1;
+  static constexpr int kStages = kDeep ? 8 : (NV == 1 ? 4 : (NV == 2 ? 3 : 2));
+  static constexpr int kMinBlocks = kDeep ? 3 : 4;
   static constexpr int SV = kThreads * NV;  // 16-byte vectors per chunk
   static constexpr int smem_bytes() { return kStages * 2 * SV * 16; }
 };
@@ -48,14 +54,14 @@ struct FwdKParams {
 };
 
 template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
-__global__ void __launch_bounds__(kThreads, 4) scan_fwd_kernel(const FwdKParams p) {
+__global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fwd_kernel(const FwdKParams p) {
   constexpr int V = Elem<T>::kVec;   // elements per 16-byte vector
   constexpr int E = V * NV;          // elements per thread per chunk
   constexpr int CH = kThreads * E;   // elements per chunk
   constexpr int LGE = ilog2(E);
   constexpr int LGCH = ilog2(CH);
-  constexpr int S = FwdCfg<NV>::kStages;
-  constexpr int SV = FwdCfg<NV>::SV;
+  constexpr int S = FwdCfg<T, NV>::kStages;
+  constexpr int SV = FwdCfg<T, NV>::SV;
 
   extern __shared__ __align__(128) uint4 dsm[];
   uint4 (*s_g)[SV] = reinterpret_cast<uint4 (*)[SV]>(dsm);           // [S][SV]
@@ -236,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 4) scan_fwd_kernel(const FwdKParams 
 // device and kernel), each a contiguous run of whole rows.
 template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
 static cudaError_t launch_fwd_t(const FwdArgs& a) {
-  constexpr int smem = FwdCfg<NV>::smem_bytes();
+  constexpr int smem = FwdCfg<T, NV>::smem_bytes();
   auto kern = scan_fwd_kernel<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>;
   static int occ_cache[64] = {0};
   int dev = 0;
