@@ -43,6 +43,10 @@ CONFIGS = {
                          tokens_scale="0.1"),
     "halfbwd_fp16": dict(batch=8, dim=2048, seqlen=8192, dtype="float16", gates="sigmoid",
                          tokens_scale="0.1"),
+    # config 4 with the gate producer fused: the kernels read z and apply
+    # exp(-softplus(z)) on load; the backward writes dz
+    "shard_bd_gated": dict(batch=16, dim=5120, seqlen=16384, dtype="bfloat16",
+                           gates="logits", tokens_scale="unit"),
     # sequence-sharded fp32 fwd+bwd, seqlen split over the ranks
     "shard_seq": dict(batch=4, dim=8192, seqlen=65536, dtype="float32", gates="0.999+0.001U",
                       tokens_scale="1/L"),
@@ -141,6 +145,8 @@ def _make_inputs(cfg, rows_lo, rows_hi, device, seed=0):
     z = torch.randn(shape, generator=gen, device=device)
     if cfg["gates"] == "exp_softplus":
         gates = torch.exp(-torch.nn.functional.softplus(z - 1.0)).to(dtype)
+    elif cfg["gates"] == "logits":  # pre-activation z ~ N(-1, 1)
+        gates = (z - 1.0).to(dtype)
     else:
         gates = torch.sigmoid(z + 2.0).to(dtype)
     del z
@@ -281,8 +287,13 @@ def run_fpscan(args, cfg):
     tokens.requires_grad_()
     n_local = (hi - lo) * L
 
+    gated = cfg["gates"] == "logits"
+
+    def fwd(g, x):
+        return fpscan_b200.pscan_gated(g, x, "exp_neg_softplus") if gated else fpscan_b200.pscan(g, x)
+
     def step():
-        y = fpscan_b200.pscan(gates, tokens)
+        y = fwd(gates, tokens)
         torch.autograd.grad(y, (gates, tokens), grad_out)
 
     stream = torch.cuda.current_stream(device)
@@ -302,7 +313,7 @@ def run_fpscan(args, cfg):
     t_start.record(stream)
     for i in range(args.steps):
         ev[i][0].record(stream)
-        y = fpscan_b200.pscan(gates, tokens)
+        y = fwd(gates, tokens)
         ev[i][1].record(stream)
         torch.autograd.grad(y, (gates, tokens), grad_out)
         ev[i][2].record(stream)
@@ -330,6 +341,25 @@ def run_fpscan(args, cfg):
     achieved_fwd = 3 * n_local * s / (fwd_mean / 1e3) / 1e9
     traffic = (int(_CFG3_BWD_TRAFFIC_PER_ELEM * n_local)
                if cfg["dtype"] in ("bfloat16", "float16") else None)
+
+    unfused = None
+    if gated:
+        # the same step composed from torch's activation + the plain scan:
+        # what the fused path replaces (same seeds, device-timed, K steps)
+        zf = gates.detach().float().requires_grad_()
+
+        def step_unfused():
+            g = torch.exp(-torch.nn.functional.softplus(zf)).to(gates.dtype)
+            y = fpscan_b200.pscan(g, tokens)
+            torch.autograd.grad(y, (zf, tokens), grad_out)
+
+        for _ in range(3):
+            step_unfused()
+        ms_u = _timed_loop(step_unfused, args.steps, stream, world)
+        unfused = {"ms_per_step": round(ms_u / args.steps, 4),
+                   "gbs_same_bytes": round(8 * rows_total * L * s * args.steps / (ms_u / 1e3) / 1e9, 2),
+                   "what": "torch exp(-softplus(z)) (fp32 z) + pscan fwd+bwd, autograd"}
+        del zf
 
     e2e = None
     if not args.no_e2e:
@@ -359,6 +389,7 @@ def run_fpscan(args, cfg):
                          "traffic": traffic,
                          "algorithmic_bytes_per_launch": 5 * n_local * s},
             "cpu_baseline": cpu,
+            "unfused_gate_composition": unfused,
             "e2e": e2e,
             "gpu_launches": 2 * args.steps,
             "clocks": clock_info,

@@ -120,6 +120,16 @@ int tuned_nv(bool forward, int dtype) {
   return forward ? 1 : 2;
 }
 
+// Gated kernels (activation fused), 16-bit types, measured at BASELINE
+// config 4: the forward does more work per element and runs faster with two
+// vectors per thread (5.7 vs 5.2 TB/s); the backward spills at two vectors
+// per thread under its register budget and runs with one (5.1 vs 3.2 TB/s).
+int tuned_nv_act(bool forward, int dtype, int act) {
+  if (act == kActNone || dtype == FPSCAN_F32 || getenv("FPSCAN_B200_NV"))
+    return tuned_nv(forward, dtype);
+  return forward ? 2 : 1;
+}
+
 constexpr int64_t kRefMinL = 32, kRefMaxL = 65536;  // csrc/full_scan/full_scan.cu:207-233
 constexpr int64_t kShardMaxL = int64_t(1) << 24;
 
@@ -151,8 +161,13 @@ int fpscan_abi_version(void) { return FPSCAN_ABI_VERSION; }
 
 const char* fpscan_last_error(void) { return t_last_error.c_str(); }
 
-int fpscan_scan_fwd(const void* gates, const void* tokens, void* out, int64_t batch, int64_t dim,
-                    int64_t seqlen, int dtype, int reverse, void* stream) {
+}  // extern "C"
+
+static int scan_fwd_impl(const void* gates, const void* tokens, void* out, int64_t batch,
+                         int64_t dim, int64_t seqlen, int dtype, int reverse, int act,
+                         void* stream) {
+  if (act < kActNone || act > kActExp)
+    return fail(FPSCAN_ERR_INVALID, "unknown gate activation code %d", act);
   int64_t rows = 0;
   FPSCAN_TRY(check_dtype(dtype));
   FPSCAN_TRY(check_shape(batch, dim, seqlen, kRefMinL, kRefMaxL, &rows));
@@ -169,8 +184,21 @@ int fpscan_scan_fwd(const void* gates, const void* tokens, void* out, int64_t ba
       return fail(FPSCAN_ERR_INVALID, "out partially overlaps %s", in->name);
   FwdArgs a{gates, tokens, out, nullptr, nullptr, nullptr, rows, seqlen, dtype,
             reverse ? 1 : 0, num_sms_current(), static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv(true, dtype);
+  a.nv = tuned_nv_act(true, dtype, act);
+  a.act = act;
   return cuda_result(launch_fwd(a), "fpscan_scan_fwd launch");
+}
+
+extern "C" {
+
+int fpscan_scan_fwd(const void* gates, const void* tokens, void* out, int64_t batch, int64_t dim,
+                    int64_t seqlen, int dtype, int reverse, void* stream) {
+  return scan_fwd_impl(gates, tokens, out, batch, dim, seqlen, dtype, reverse, kActNone, stream);
+}
+
+int fpscan_scan_fwd_act(const void* z, const void* tokens, void* out, int64_t batch, int64_t dim,
+                        int64_t seqlen, int dtype, int reverse, int activation, void* stream) {
+  return scan_fwd_impl(z, tokens, out, batch, dim, seqlen, dtype, reverse, activation, stream);
 }
 
 int64_t fpscan_scan_fwd_workspace_bytes(int64_t batch, int64_t dim, int64_t seqlen, int dtype) {
@@ -213,9 +241,13 @@ int fpscan_scan_fwd_ws(const void* gates, const void* tokens, void* out, int64_t
   return cuda_result(launch_split(a), "fpscan_scan_fwd_ws launch");
 }
 
-int fpscan_scan_bwd(const void* gates, const void* y, const void* grad_out, void* dgates,
-                    void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
-                    void* stream) {
+}  // extern "C"
+
+static int scan_bwd_impl(const void* gates, const void* y, const void* grad_out, void* dgates,
+                         void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                         int act, void* stream) {
+  if (act < kActNone || act > kActExp)
+    return fail(FPSCAN_ERR_INVALID, "unknown gate activation code %d", act);
   int64_t rows = 0;
   FPSCAN_TRY(check_dtype(dtype));
   FPSCAN_TRY(check_shape(batch, dim, seqlen, kRefMinL, kRefMaxL, &rows));
@@ -238,8 +270,24 @@ int fpscan_scan_bwd(const void* gates, const void* y, const void* grad_out, void
   BwdArgs a{gates,   y,       grad_out, dgates, dtokens, nullptr, nullptr,
             nullptr, rows,    seqlen,   dtype,  num_sms_current(),
             static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv(false, dtype);
+  a.nv = tuned_nv_act(false, dtype, act);
+  a.act = act;
   return cuda_result(launch_bwd(a), "fpscan_scan_bwd launch");
+}
+
+extern "C" {
+
+int fpscan_scan_bwd(const void* gates, const void* y, const void* grad_out, void* dgates,
+                    void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                    void* stream) {
+  return scan_bwd_impl(gates, y, grad_out, dgates, dtokens, batch, dim, seqlen, dtype, kActNone,
+                       stream);
+}
+
+int fpscan_scan_bwd_act(const void* z, const void* y, const void* grad_out, void* dz,
+                        void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                        int activation, void* stream) {
+  return scan_bwd_impl(z, y, grad_out, dz, dtokens, batch, dim, seqlen, dtype, activation, stream);
 }
 
 int fpscan_scan_fwd_init(const void* gates, const void* tokens, void* out, const float* init,

@@ -225,6 +225,47 @@ __device__ __forceinline__ uint4 pack_vec<__half>(const float* v) {
   return r;
 }
 
+// Gate activations fused into the loads: the kernels read pre-activation
+// values z and use g = act(z), computed in fp32.  exp(-softplus(z)) =
+// 1 / (1 + e^z) is the sigmoid of -z.  act_grad gives dg/dz from g.
+enum Act : int { kActNone = 0, kActSigmoid = 1, kActExpNegSoftplus = 2, kActExp = 3 };
+
+// Hardware tanh (one MUFU op; relative error about 2^-11).
+__device__ __forceinline__ float tanh_approx(float x) {
+  float r;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// For fp32 data the sigmoids use the fast exp and divide intrinsics (a few
+// ulp).  For fp16 / bf16 data, sigmoid(x) = 0.5 + 0.5 tanh(x / 2) costs one
+// MUFU op; its error is well below the 2^-8 / 2^-11 rounding of the gate
+// that an unfused producer would store in the input type.  (__fdividef
+// returns 0 when the denominator overflows to inf, the correct limit.)
+template <int ACT, typename T>
+__device__ __forceinline__ float act_fwd(float z) {
+  constexpr bool kHalf = sizeof(T) == 2;
+  if constexpr (ACT == kActSigmoid) {
+    if constexpr (kHalf) return fmaf(0.5f, tanh_approx(0.5f * z), 0.5f);
+    else return __fdividef(1.f, 1.f + __expf(-z));
+  } else if constexpr (ACT == kActExpNegSoftplus) {
+    if constexpr (kHalf) return fmaf(-0.5f, tanh_approx(0.5f * z), 0.5f);
+    else return __fdividef(1.f, 1.f + __expf(z));
+  } else if constexpr (ACT == kActExp) {
+    return __expf(z);
+  } else {
+    return z;
+  }
+}
+
+template <int ACT>
+__device__ __forceinline__ float act_grad(float g) {
+  if constexpr (ACT == kActSigmoid) return g * (1.f - g);
+  else if constexpr (ACT == kActExpNegSoftplus) return -g * (1.f - g);
+  else if constexpr (ACT == kActExp) return g;
+  else return 1.f;
+}
+
 constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v >> 1); }
 
 }  // namespace fpscan

@@ -31,6 +31,7 @@ struct FwdArgs {
   int num_sms;
   cudaStream_t stream;
   int nv = 2;           // 16-byte vectors per thread per chunk (1 or 2)
+  int act = 0;          // gate activation applied on load (Act); plain scan only
 };
 
 struct BwdArgs {
@@ -48,6 +49,7 @@ struct BwdArgs {
   int num_sms;
   cudaStream_t stream;
   int nv = 2;           // 16-byte vectors per thread per chunk (1 or 2)
+  int act = 0;          // gate activation (Act): dgates becomes d/dz; plain backward only
 };
 
 struct SplitArgs {

@@ -50,7 +50,7 @@ struct BwdKParams {
   int lg;
 };
 
-template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY>
+template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY, int ACT>
 __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks) scan_bwd_kernel(const BwdKParams p) {
   constexpr int V = Elem<T>::kVec;
   constexpr int E = V * NV;
@@ -162,7 +162,8 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks) scan_bwd_ker
         gov[q].raw = rgo[q];
         if (HAS_OUT) yv[q].raw = ry[q];
       }
-      if (valid && !grp_row_end) g_next = Elem<T>::load(reinterpret_cast<const T*>(sg + NV)[0]);
+      if (valid && !grp_row_end)
+        g_next = act_fwd<ACT, T>(Elem<T>::load(reinterpret_cast<const T*>(sg + NV)[0]));
       if (HAS_OUT && valid && !grp_row_first)
         y_before = Elem<T>::load(reinterpret_cast<const T*>(sy)[-1]);
     }
@@ -170,7 +171,8 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks) scan_bwd_ker
 #pragma unroll
       for (int i = 0; i < E; ++i) {
         const int j = E - 1 - i;  // element within the thread's group, memory order
-        const float g = (j == E - 1) ? g_next : Elem<T>::load(gv[(j + 1) / V].e[(j + 1) % V]);
+        const float g = (j == E - 1) ? g_next
+                                      : act_fwd<ACT, T>(Elem<T>::load(gv[(j + 1) / V].e[(j + 1) % V]));
         const float x = Elem<T>::load(gov[j / V].e[j % V]);
         if (i == 0) {
           a[0] = g;
@@ -236,7 +238,14 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks) scan_bwd_ker
           const int j = E - 1 - i;
           const float yp = (j == 0) ? yp_first : Elem<T>::load(yv[(j - 1) / V].e[(j - 1) % V]);
           f_dt[j] = dt[i];
-          f_dg[j] = dt[i] * yp;
+          if constexpr (ACT == kActNone) {
+            f_dg[j] = dt[i] * yp;
+          } else {
+            // recomputed rather than kept from the scan loop: E more live
+            // registers would spill at this kernel's register budget
+            const float gj = act_fwd<ACT, T>(Elem<T>::load(gv[j / V].e[j % V]));
+            f_dg[j] = dt[i] * yp * act_grad<ACT>(gj);
+          }
         }
         uint4* d1 = reinterpret_cast<uint4*>(dtok + base + off) + vi * NV;
         uint4* d2 = reinterpret_cast<uint4*>(dgates + base + off) + vi * NV;
@@ -246,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks) scan_bwd_ker
           d2[q] = pack_vec<T>(f_dg + q * V);
         }
       } else if (grp_row_first) {
-        p.carry_b[row] = Elem<T>::load(gv[0].e[0]) * dt[E - 1];
+        p.carry_b[row] = Elem<T>::load(gv[0].e[0]) * dt[E - 1];  // plain scan only
       }
     }
 
@@ -264,10 +273,10 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks) scan_bwd_ker
   }
 }
 
-template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY>
+template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY, int ACT>
 static cudaError_t launch_bwd_t(const BwdArgs& a) {
   constexpr int smem = BwdCfg<NV>::template smem_bytes<HAS_OUT>();
-  auto kern = scan_bwd_kernel<T, NV, HAS_OUT, HAS_CARRY>;
+  auto kern = scan_bwd_kernel<T, NV, HAS_OUT, HAS_CARRY, ACT>;
   // Per device: opt in to >48 KiB of dynamic shared memory and cache the
   // number of resident CTAs.
   static int occ_cache[64] = {0};
@@ -293,20 +302,32 @@ static cudaError_t launch_bwd_t(const BwdArgs& a) {
   return cudaGetLastError();
 }
 
-template <typename T, bool HAS_OUT, bool HAS_CARRY>
+template <typename T, bool HAS_OUT, bool HAS_CARRY, int ACT = kActNone>
 static cudaError_t launch_bwd_nv(const BwdArgs& a) {
-  if constexpr (sizeof(T) == 4)
-    if (a.nv == 4) return launch_bwd_t<T, 4, HAS_OUT, HAS_CARRY>(a);
-  return a.nv == 1 ? launch_bwd_t<T, 1, HAS_OUT, HAS_CARRY>(a)
-                   : launch_bwd_t<T, 2, HAS_OUT, HAS_CARRY>(a);
+  if constexpr (sizeof(T) == 4 && ACT == kActNone)
+    if (a.nv == 4) return launch_bwd_t<T, 4, HAS_OUT, HAS_CARRY, ACT>(a);
+  return a.nv == 1 ? launch_bwd_t<T, 1, HAS_OUT, HAS_CARRY, ACT>(a)
+                   : launch_bwd_t<T, 2, HAS_OUT, HAS_CARRY, ACT>(a);
 }
 
 template <typename T>
 static cudaError_t launch_bwd_dtype(const BwdArgs& a) {
   const bool has_out = a.dtokens != nullptr;
   const bool has_carry = a.addend != nullptr;
-  if (has_out)
-    return has_carry ? launch_bwd_nv<T, true, true>(a) : launch_bwd_nv<T, true, false>(a);
+  if (has_out && !has_carry) {
+    switch (a.act) {
+      case kActSigmoid:
+        return launch_bwd_nv<T, true, false, kActSigmoid>(a);
+      case kActExpNegSoftplus:
+        return launch_bwd_nv<T, true, false, kActExpNegSoftplus>(a);
+      case kActExp:
+        return launch_bwd_nv<T, true, false, kActExp>(a);
+      default:
+        return launch_bwd_nv<T, true, false>(a);
+    }
+  }
+  if (a.act != kActNone) return cudaErrorInvalidValue;
+  if (has_out) return launch_bwd_nv<T, true, true>(a);
   return launch_bwd_nv<T, false, false>(a);
 }
 

@@ -53,7 +53,8 @@ struct FwdKParams {
   int lg;  // log2(seqlen)
 };
 
-template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
+template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT,
+          int ACT>
 __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fwd_kernel(const FwdKParams p) {
   constexpr int V = Elem<T>::kVec;   // elements per 16-byte vector
   constexpr int E = V * NV;          // elements per thread per chunk
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
 #pragma unroll
       for (int i = 0; i < E; ++i) {
         const int j = REV ? E - 1 - i : i;
-        const float g = Elem<T>::load(gv[j / V].e[j % V]);
+        const float g = act_fwd<ACT, T>(Elem<T>::load(gv[j / V].e[j % V]));
         const float x = Elem<T>::load(xv[j / V].e[j % V]);
         if (i == 0) {
           a[0] = g;
@@ -240,10 +241,11 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
 
 // One wave of CTAs: tiles = SMs x resident CTAs per SM (queried once per
 // device and kernel), each a contiguous run of whole rows.
-template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
+template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT,
+          int ACT>
 static cudaError_t launch_fwd_t(const FwdArgs& a) {
   constexpr int smem = FwdCfg<T, NV>::smem_bytes();
-  auto kern = scan_fwd_kernel<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>;
+  auto kern = scan_fwd_kernel<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT>;
   static int occ_cache[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -267,12 +269,26 @@ static cudaError_t launch_fwd_t(const FwdArgs& a) {
   return cudaGetLastError();
 }
 
-template <typename T, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT>
+template <typename T, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT, int ACT = kActNone>
 static cudaError_t launch_fwd_nv(const FwdArgs& a) {
-  if constexpr (sizeof(T) == 4)
-    if (a.nv == 4) return launch_fwd_t<T, 4, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>(a);
-  return a.nv == 1 ? launch_fwd_t<T, 1, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>(a)
-                   : launch_fwd_t<T, 2, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT>(a);
+  if constexpr (sizeof(T) == 4 && ACT == kActNone)
+    if (a.nv == 4) return launch_fwd_t<T, 4, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT>(a);
+  return a.nv == 1 ? launch_fwd_t<T, 1, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT>(a)
+                   : launch_fwd_t<T, 2, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT>(a);
+}
+
+template <typename T, bool REV>
+static cudaError_t launch_fwd_act(const FwdArgs& a) {
+  switch (a.act) {
+    case kActSigmoid:
+      return launch_fwd_nv<T, REV, true, false, false, kActSigmoid>(a);
+    case kActExpNegSoftplus:
+      return launch_fwd_nv<T, REV, true, false, false, kActExpNegSoftplus>(a);
+    case kActExp:
+      return launch_fwd_nv<T, REV, true, false, false, kActExp>(a);
+    default:
+      return launch_fwd_nv<T, REV, true, false, false>(a);
+  }
 }
 
 template <typename T>
@@ -283,8 +299,8 @@ static cudaError_t launch_fwd_dtype(const FwdArgs& a) {
   // Instantiated variants: plain scan (fwd/rev); forward with init
   // (+carry-out); carry-out only (reduce).
   if (has_out && !has_init && !has_co)
-    return a.reverse ? launch_fwd_nv<T, true, true, false, false>(a)
-                     : launch_fwd_nv<T, false, true, false, false>(a);
+    return a.reverse ? launch_fwd_act<T, true>(a) : launch_fwd_act<T, false>(a);
+  if (a.act != kActNone) return cudaErrorInvalidValue;
   if (has_out && has_init && !has_co)
     return a.reverse ? launch_fwd_nv<T, true, true, true, false>(a)
                      : launch_fwd_nv<T, false, true, true, false>(a);

@@ -22,7 +22,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["pscan", "scan_forward", "PScan"]
+__all__ = ["pscan", "scan_forward", "PScan", "pscan_gated", "scan_forward_gated"]
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 MIN_SEQLEN = 32
@@ -223,3 +223,64 @@ def pscan(gates: torch.Tensor, tokens: torch.Tensor,
     if initial_state is None:
         return PScan.apply(gates, tokens)
     return PScanWithState.apply(gates, tokens, initial_state)
+
+
+# --------------------------------------------------------------------------- fused gate producers
+GATE_ACTIVATIONS = {"sigmoid": 1, "exp_neg_softplus": 2, "exp": 3}
+
+
+def _act_code(activation: str) -> int:
+    try:
+        return GATE_ACTIVATIONS[activation]
+    except KeyError:
+        raise RuntimeError(f"activation must be one of {sorted(GATE_ACTIVATIONS)}, "
+                           f"got {activation!r}") from None
+
+
+def scan_forward_gated(z: torch.Tensor, tokens: torch.Tensor, activation: str = "sigmoid",
+                       reverse: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``scan_forward(act(z), tokens)`` with the gate activation applied
+    inside the scan kernel (no separate pass over z).  ``activation``:
+    "sigmoid", "exp_neg_softplus" (exp(-softplus(z)) = sigmoid(-z)) or "exp"."""
+    code = _act_code(activation)
+    validate(z, tokens, out)
+    if out is None:
+        out = torch.empty_like(tokens)
+    b, d, l = tokens.shape
+    with torch.cuda.device(tokens.device):
+        _lib.call("fpscan_scan_fwd_act", z.data_ptr(), tokens.data_ptr(), out.data_ptr(), b, d, l,
+                  DTYPE_CODES[tokens.dtype], 1 if reverse else 0, code,
+                  _stream_ptr(tokens.device))
+    return out
+
+
+class PScanGated(torch.autograd.Function):
+    """Differentiable scan of gates = act(z): one forward kernel, one fused
+    backward kernel producing (grad_z, grad_tokens)."""
+
+    @staticmethod
+    def forward(ctx, z, tokens, activation):
+        out = scan_forward_gated(z, tokens, activation)
+        ctx.save_for_backward(z, out)
+        ctx.code = _act_code(activation)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        z, out = ctx.saved_tensors
+        grad_output = grad_output.contiguous()
+        validate(z, grad_output)
+        dz = torch.empty_like(grad_output)
+        dtokens = torch.empty_like(grad_output)
+        b, d, l = grad_output.shape
+        with torch.cuda.device(grad_output.device):
+            _lib.call("fpscan_scan_bwd_act", z.data_ptr(), out.data_ptr(), grad_output.data_ptr(),
+                      dz.data_ptr(), dtokens.data_ptr(), b, d, l, DTYPE_CODES[grad_output.dtype],
+                      ctx.code, _stream_ptr(grad_output.device))
+        return dz, dtokens, None
+
+
+def pscan_gated(z: torch.Tensor, tokens: torch.Tensor, activation: str = "sigmoid") -> torch.Tensor:
+    """Differentiable ``pscan(act(z), tokens)`` with the gate producer fused
+    into the scan kernels (forward and backward)."""
+    return PScanGated.apply(z, tokens, activation)

@@ -82,6 +82,32 @@ FPSCAN_API int fpscan_scan_fwd_ws(const void* gates, const void* tokens, void* o
                                   int reverse, void* workspace, int64_t workspace_bytes,
                                   void* stream);
 
+/* Gate activations for the *_act entry points: the kernels read
+ * pre-activation values z and use gates = act(z) (computed in fp32). */
+#define FPSCAN_ACT_NONE 0
+#define FPSCAN_ACT_SIGMOID 1           /* gates = 1 / (1 + exp(-z))            */
+#define FPSCAN_ACT_EXP_NEG_SOFTPLUS 2  /* gates = exp(-softplus(z)) = 1/(1+e^z) */
+#define FPSCAN_ACT_EXP 3               /* gates = exp(z)                        */
+
+/*
+ * fpscan_scan_fwd on gates = act(z): the activation that produces the gates
+ * (e.g. sigmoid, or BASELINE config 4's exp(-softplus(z))) is applied as the
+ * chunk is loaded, so the separate elementwise pass over z (read z, write
+ * gates) disappears.  No reference counterpart (extends fullscan_forward).
+ */
+FPSCAN_API int fpscan_scan_fwd_act(const void* z, const void* tokens, void* out, int64_t batch,
+                                   int64_t dim, int64_t seqlen, int dtype, int reverse,
+                                   int activation, void* stream);
+
+/*
+ * fpscan_scan_bwd for y = scan(act(z), tokens): writes dz = dgates * act'(z)
+ * instead of dgates (the producer's backward fused in), and dtokens.
+ * No reference counterpart.
+ */
+FPSCAN_API int fpscan_scan_bwd_act(const void* z, const void* y, const void* grad_out, void* dz,
+                                   void* dtokens, int64_t batch, int64_t dim, int64_t seqlen,
+                                   int dtype, int activation, void* stream);
+
 /*
  * Scan with a per-row initial state `init` (fp32, batch*dim values):
  * y[0] = gates[0]*init + tokens[0] (reverse: y[L-1] = gates[L-1]*init +

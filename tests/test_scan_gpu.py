@@ -526,3 +526,62 @@ def test_initial_state_gradients(dtype, seqlen):
     check(x.grad, x64.grad.numpy(), dtype, "dtokens")
     check(g.grad, g64.grad.numpy(), dtype, "dgates")
     check(h.grad, h64.grad.numpy(), dtype, "dh0")
+
+
+# ----------------------------------------------------------------- fused gate producers
+_ACTS = {
+    "sigmoid": (lambda z: 1 / (1 + np.exp(-z)), lambda g: g * (1 - g)),
+    "exp_neg_softplus": (lambda z: np.exp(-np.logaddexp(0, z)), lambda g: -g * (1 - g)),
+    "exp": (np.exp, lambda g: g),
+}
+
+
+@pytest.mark.parametrize("activation", sorted(_ACTS))
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("seqlen", [32, 1024, 16384])
+def test_gated_scan_fwd_bwd(activation, dtype, seqlen):
+    gen = torch.Generator(device=DEVICE).manual_seed(seqlen + 53)
+    shape = (2, 5, seqlen)
+    if activation == "exp":
+        z = (-0.02 * torch.rand(shape, generator=gen, device=DEVICE)).to(dtype)
+    elif activation == "sigmoid":
+        z = (torch.randn(shape, generator=gen, device=DEVICE) + 4).to(dtype)
+    else:
+        z = (torch.randn(shape, generator=gen, device=DEVICE) - 4).to(dtype)
+    x = (torch.randn(shape, generator=gen, device=DEVICE) * 0.1).to(dtype)
+    go = torch.randn(shape, generator=gen, device=DEVICE).to(dtype)
+    act, dact = _ACTS[activation]
+    g64 = act(_np64(z))
+    for rev in (False, True):
+        y = fpscan.scan_forward_gated(z, x, activation, reverse=rev)
+        _check(y, oracle.scan_f64(g64, _np64(x), rev), dtype, f"{activation} rev={rev}")
+    zz, xx = z.clone().requires_grad_(), x.clone().requires_grad_()
+    y = fpscan.pscan_gated(zz, xx, activation)
+    dz, dt = torch.autograd.grad(y, (zz, xx), go)
+    y64 = oracle.scan_f64(g64, _np64(x))
+    dg64, dt64 = oracle.scan_bwd_f64(g64, y64, _np64(go))
+    _check(dt, dt64, dtype, "dtokens")
+    _assert_normwise(dz, dg64 * dact(g64), dtype, "dz")
+    if dtype == torch.float32:
+        _check(dz, dg64 * dact(g64), dtype, "dz")
+
+
+def test_gated_scan_matches_unfused_composition():
+    """Config-4 distributions at a small size: fused exp(-softplus) against
+    torch's activation followed by the plain scan and backward."""
+    gen = torch.Generator(device=DEVICE).manual_seed(7)
+    shape = (4, 96, 16384)
+    z = (torch.randn(shape, generator=gen, device=DEVICE) - 1).to(torch.bfloat16)
+    x = torch.randn(shape, generator=gen, device=DEVICE).to(torch.bfloat16)
+    go = torch.randn(shape, generator=gen, device=DEVICE).to(torch.bfloat16)
+    zz = z.clone().requires_grad_()
+    xx = x.clone().requires_grad_()
+    y = fpscan.pscan_gated(zz, xx, "exp_neg_softplus")
+    dz, dt = torch.autograd.grad(y, (zz, xx), go)
+    z2 = z.float().clone().requires_grad_()
+    x2 = x.clone().requires_grad_()
+    g = torch.exp(-torch.nn.functional.softplus(z2)).to(torch.bfloat16)
+    y2 = fpscan.pscan(g, x2)
+    dz2, dt2 = torch.autograd.grad(y2, (z2, x2), go)
+    for a, b in ((y, y2), (dt, dt2), (dz, dz2)):
+        assert oracle.normwise_error(_np64(a), _np64(b)) <= 2e-2
