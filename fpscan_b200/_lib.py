@@ -28,6 +28,8 @@ SIGNATURES = {
     "fpscan_scan_fwd_init": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
     "fpscan_scan_fwd_act": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _vp],
     "fpscan_scan_bwd_act": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
+    "fpscan_scan_fwd_anylen": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
+    "fpscan_scan_bwd_anylen": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_scan_bwd": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_fwd_reduce": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_fwd_scan": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],

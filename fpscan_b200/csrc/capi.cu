@@ -96,6 +96,24 @@ int check_shape(int64_t batch, int64_t dim, int64_t seqlen, int64_t min_l, int64
   return FPSCAN_OK;
 }
 
+// Shape check of the any-seqlen entry points: seqlen >= 1, no power-of-two
+// or upper limit beyond what 64-bit offsets and the grid allow.
+int check_shape_any(int64_t batch, int64_t dim, int64_t seqlen, int64_t* rows) {
+  if (batch < 0 || dim < 0)
+    return fail(FPSCAN_ERR_INVALID, "batch (%lld) and dim (%lld) must be non-negative",
+                (long long)batch, (long long)dim);
+  if (seqlen < 1) return fail(FPSCAN_ERR_INVALID, "seqlen must be >= 1 (got %lld)", (long long)seqlen);
+  if (dim != 0 && batch > INT64_MAX / dim)
+    return fail(FPSCAN_ERR_INVALID, "batch*dim overflows");
+  const int64_t r = batch * dim;
+  if (r != 0 && r > INT64_MAX / seqlen / 8)
+    return fail(FPSCAN_ERR_INVALID, "tensor too large");
+  if (r > (int64_t)0x7fffffff * 64)
+    return fail(FPSCAN_ERR_INVALID, "batch*dim too large for the launch grid");
+  *rows = r;
+  return FPSCAN_OK;
+}
+
 int cuda_result(cudaError_t e, const char* what) {
   if (e != cudaSuccess)
     return fail(FPSCAN_ERR_CUDA, "%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
@@ -406,6 +424,85 @@ int fpscan_device_status(unsigned* status, int clear) {
   }
   *status = v;
   return ok();
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int fpscan_scan_fwd_anylen(const void* gates, const void* tokens, void* out, int64_t batch,
+                           int64_t dim, int64_t seqlen, int dtype, int reverse, void* stream) {
+  int64_t rows = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape_any(batch, dim, seqlen, &rows));
+  if (rows == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(tokens, "tokens"));
+  FPSCAN_TRY(check_ptr(out, "out"));
+  const uintptr_t bytes = (uintptr_t)(rows * seqlen * dtype_size(dtype));
+  const Span so{"out", (uintptr_t)out, (uintptr_t)out + bytes};
+  const Span sg{"gates", (uintptr_t)gates, (uintptr_t)gates + bytes};
+  const Span st{"tokens", (uintptr_t)tokens, (uintptr_t)tokens + bytes};
+  for (const Span* in : {&sg, &st})
+    if (overlaps(so, *in) && so.lo != in->lo)
+      return fail(FPSCAN_ERR_INVALID, "out partially overlaps %s", in->name);
+  AnyArgs a{};
+  a.gates = gates;
+  a.tokens = tokens;
+  a.out = out;
+  a.rows = rows;
+  a.seqlen = seqlen;
+  a.dtype = dtype;
+  a.reverse = reverse ? 1 : 0;
+  a.backward = 0;
+  a.num_sms = num_sms_current();
+  a.stream = static_cast<cudaStream_t>(stream);
+  // measured on B200 (bf16 / fp32, (8, 2048, 8191) and (16, 5120, 16383)):
+  // two vectors per thread, 5.3-5.7 TB/s bf16 vs 4.3 with one
+  a.nv = 2;
+  if (const char* v = getenv("FPSCAN_B200_ANY_FWD_NV")) a.nv = v[0] == '1' ? 1 : 2;
+  return cuda_result(launch_anylen(a), "fpscan_scan_fwd_anylen launch");
+}
+
+int fpscan_scan_bwd_anylen(const void* gates, const void* y, const void* grad_out, void* dgates,
+                           void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                           void* stream) {
+  int64_t rows = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape_any(batch, dim, seqlen, &rows));
+  if (rows == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(y, "y"));
+  FPSCAN_TRY(check_ptr(grad_out, "grad_out"));
+  FPSCAN_TRY(check_ptr(dgates, "dgates"));
+  FPSCAN_TRY(check_ptr(dtokens, "dtokens"));
+  const uintptr_t bytes = (uintptr_t)(rows * seqlen * dtype_size(dtype));
+  const Span in[3] = {{"gates", (uintptr_t)gates, (uintptr_t)gates + bytes},
+                      {"y", (uintptr_t)y, (uintptr_t)y + bytes},
+                      {"grad_out", (uintptr_t)grad_out, (uintptr_t)grad_out + bytes}};
+  const Span o[2] = {{"dgates", (uintptr_t)dgates, (uintptr_t)dgates + bytes},
+                     {"dtokens", (uintptr_t)dtokens, (uintptr_t)dtokens + bytes}};
+  if (overlaps(o[0], o[1])) return fail(FPSCAN_ERR_INVALID, "dgates overlaps dtokens");
+  for (const Span& os : o)
+    for (const Span& is : in)
+      if (overlaps(os, is)) return fail(FPSCAN_ERR_INVALID, "%s overlaps %s", os.name, is.name);
+  AnyArgs a{};
+  a.gates = gates;
+  a.y = y;
+  a.grad_out = grad_out;
+  a.dgates = dgates;
+  a.dtokens = dtokens;
+  a.rows = rows;
+  a.seqlen = seqlen;
+  a.dtype = dtype;
+  a.backward = 1;
+  a.num_sms = num_sms_current();
+  a.stream = static_cast<cudaStream_t>(stream);
+  // fp32: two vectors per thread (6.3-6.4 TB/s vs 5.3); 16-bit types: one
+  // (two spill under the register budget: 3.8 vs 5.0 TB/s)
+  a.nv = dtype == FPSCAN_F32 ? 2 : 1;
+  if (const char* v = getenv("FPSCAN_B200_ANY_BWD_NV")) a.nv = v[0] == '2' ? 2 : 1;
+  return cuda_result(launch_anylen(a), "fpscan_scan_bwd_anylen launch");
 }
 
 }  // extern "C"

@@ -65,6 +65,25 @@ struct SplitArgs {
   cudaStream_t stream;
 };
 
+// Scan / backward for any seqlen >= 1 (scan_anylen.cu).
+struct AnyArgs {
+  const void* gates;
+  const void* tokens;    // forward
+  void* out;             // forward
+  const void* y;         // backward: forward output
+  const void* grad_out;  // backward
+  void* dgates;          // backward
+  void* dtokens;         // backward
+  int64_t rows;
+  int64_t seqlen;
+  int dtype;
+  int reverse;           // forward only
+  int backward;
+  int num_sms;
+  cudaStream_t stream;
+  int nv = 1;            // 16-byte vectors per thread per chunk (1 or 2)
+};
+
 // Records `fmt` as this thread's fpscan_last_error() message; returns code.
 int set_error(int code, const char* fmt, ...);
 
@@ -74,6 +93,7 @@ int split_slots(int dtype, int num_sms);
 int split_segments(int64_t rows, int64_t seqlen, int dtype, int slots);
 int64_t split_workspace_bytes(int64_t rows, int segments);
 cudaError_t launch_bwd(const BwdArgs& a);
+cudaError_t launch_anylen(const AnyArgs& a);
 cudaError_t launch_carry_combine(const float* gathered, int world, int rank, int64_t rows,
                                  int reverse, float* out, cudaStream_t stream);
 

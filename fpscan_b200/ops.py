@@ -22,7 +22,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["pscan", "scan_forward", "PScan", "pscan_gated", "scan_forward_gated"]
+__all__ = ["pscan", "scan_forward", "PScan", "pscan_gated", "scan_forward_gated",
+           "pscan_anylen", "scan_forward_anylen"]
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 MIN_SEQLEN = 32
@@ -42,16 +43,17 @@ def _check_input(x: torch.Tensor, name: str) -> None:
 
 
 def validate(gates: torch.Tensor, tokens: torch.Tensor,
-             out: Optional[torch.Tensor] = None) -> None:
+             out: Optional[torch.Tensor] = None, any_seqlen: bool = False) -> None:
     """Raise RuntimeError unless (gates, tokens[, out]) form a valid scan call."""
     _check_input(gates, "gates")
     _check_input(tokens, "tokens")
-    validate_layout(gates, tokens, out)
+    validate_layout(gates, tokens, out, any_seqlen)
 
 
 def validate_layout(gates: torch.Tensor, tokens: torch.Tensor,
-                    out: Optional[torch.Tensor] = None) -> None:
-    """Device-independent checks (shape, dtype, seqlen, out); CPU-testable."""
+                    out: Optional[torch.Tensor] = None, any_seqlen: bool = False) -> None:
+    """Device-independent checks (shape, dtype, seqlen, out); CPU-testable.
+    ``any_seqlen`` accepts every seqlen >= 1 (the *_anylen functions)."""
     if tokens.dim() != 3:
         raise RuntimeError(f"tokens must be 3-D (batch, dim, seqlen), got {tuple(tokens.shape)}")
     if gates.shape != tokens.shape:
@@ -62,7 +64,10 @@ def validate_layout(gates: torch.Tensor, tokens: torch.Tensor,
     if gates.device != tokens.device:
         raise RuntimeError("gates and tokens must be on the same device")
     seqlen = tokens.shape[-1]
-    if seqlen & (seqlen - 1) or not MIN_SEQLEN <= seqlen <= MAX_SEQLEN:
+    if any_seqlen:
+        if seqlen < 1:
+            raise RuntimeError(f"seqlen must be >= 1 (got {seqlen})")
+    elif seqlen & (seqlen - 1) or not MIN_SEQLEN <= seqlen <= MAX_SEQLEN:
         raise RuntimeError(
             f"seqlen must be a power of 2, >= {MIN_SEQLEN}, <= {MAX_SEQLEN} (got {seqlen})")
     if out is not None:
@@ -284,3 +289,55 @@ def pscan_gated(z: torch.Tensor, tokens: torch.Tensor, activation: str = "sigmoi
     """Differentiable ``pscan(act(z), tokens)`` with the gate producer fused
     into the scan kernels (forward and backward)."""
     return PScanGated.apply(z, tokens, activation)
+
+
+# --------------------------------------------------------------------------- any seqlen
+def scan_forward_anylen(gates: torch.Tensor, tokens: torch.Tensor, reverse: bool = False,
+                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``scan_forward`` for any seqlen >= 1: not limited to the reference's
+    powers of two in [32, 65536] (csrc/full_scan/full_scan.cu:207-233).
+    Zero initial state; ``reverse`` and ``out`` as in ``scan_forward``."""
+    _lib.load()
+    validate(gates, tokens, out, any_seqlen=True)
+    if out is None:
+        out = torch.empty_like(tokens)
+    b, d, l = tokens.shape
+    with torch.cuda.device(tokens.device):
+        _lib.call("fpscan_scan_fwd_anylen", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
+                  b, d, l, DTYPE_CODES[tokens.dtype], 1 if reverse else 0,
+                  _stream_ptr(tokens.device))
+    return out
+
+
+def scan_backward_anylen(gates: torch.Tensor, out: torch.Tensor, grad_output: torch.Tensor):
+    """Fused backward of ``pscan_anylen``: returns (grad_gates, grad_tokens)."""
+    validate(gates, grad_output, any_seqlen=True)
+    validate(out, grad_output, any_seqlen=True)
+    dgates = torch.empty_like(grad_output)
+    dtokens = torch.empty_like(grad_output)
+    b, d, l = grad_output.shape
+    with torch.cuda.device(grad_output.device):
+        _lib.call("fpscan_scan_bwd_anylen", gates.data_ptr(), out.data_ptr(),
+                  grad_output.data_ptr(), dgates.data_ptr(), dtokens.data_ptr(), b, d, l,
+                  DTYPE_CODES[grad_output.dtype], _stream_ptr(grad_output.device))
+    return dgates, dtokens
+
+
+class PScanAnyLen(torch.autograd.Function):
+    """``PScan`` for any seqlen >= 1."""
+
+    @staticmethod
+    def forward(ctx, gates, tokens):
+        out = scan_forward_anylen(gates, tokens)
+        ctx.save_for_backward(gates, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        gates, out = ctx.saved_tensors
+        return scan_backward_anylen(gates, out, grad_output.contiguous())
+
+
+def pscan_anylen(gates: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
+    """Differentiable ``pscan`` for any seqlen >= 1 (e.g. 1000, 3, 200000)."""
+    return PScanAnyLen.apply(gates, tokens)

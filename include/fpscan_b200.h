@@ -109,6 +109,26 @@ FPSCAN_API int fpscan_scan_bwd_act(const void* z, const void* y, const void* gra
                                    int dtype, int activation, void* stream);
 
 /*
+ * fpscan_scan_fwd for ANY seqlen >= 1.  The reference accepts only powers of
+ * two in [32, 65536] (csrc/full_scan/full_scan.cu:207-233, README.md:101-106);
+ * this entry point has no counterpart there and lifts that limit (masked row
+ * tails; rows need not start on a 16-byte boundary, only the three base
+ * pointers must be 16-byte aligned).  Zero initial state, `out` may equal
+ * `gates` or `tokens`, otherwise as fpscan_scan_fwd.
+ */
+FPSCAN_API int fpscan_scan_fwd_anylen(const void* gates, const void* tokens, void* out,
+                                      int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                                      int reverse, void* stream);
+
+/*
+ * fpscan_scan_bwd (the fused PScan.backward, fpscan/ops.py:70-83) for any
+ * seqlen >= 1.  No reference counterpart.  Outputs must not overlap inputs.
+ */
+FPSCAN_API int fpscan_scan_bwd_anylen(const void* gates, const void* y, const void* grad_out,
+                                      void* dgates, void* dtokens, int64_t batch, int64_t dim,
+                                      int64_t seqlen, int dtype, void* stream);
+
+/*
  * Scan with a per-row initial state `init` (fp32, batch*dim values):
  * y[0] = gates[0]*init + tokens[0] (reverse: y[L-1] = gates[L-1]*init +
  * tokens[L-1]).  The final state is the last element of out in scan order.

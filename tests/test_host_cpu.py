@@ -123,3 +123,26 @@ def test_reference_style_extension_shim():
     from fpscan_b200 import _C
 
     assert hasattr(_C, "fullscan_forward")
+
+
+def test_anylen_validation_and_c_abi_checks():
+    # any seqlen >= 1 is accepted by the *_anylen layer; 0 is not
+    for l in [1, 3, 1000, 65537, 300001]:
+        t = torch.empty(1, 1, l)
+        ops.validate_layout(t, t, torch.empty_like(t), any_seqlen=True)
+    t = torch.empty(1, 1, 0)
+    with pytest.raises(RuntimeError):
+        ops.validate_layout(t, t, any_seqlen=True)
+    with pytest.raises(RuntimeError):  # strict path unchanged
+        ops.validate_layout(torch.empty(1, 1, 1000), torch.empty(1, 1, 1000))
+    lib = _lib.load()
+    assert lib.fpscan_scan_fwd_anylen(16, 16, 16, 1, 1, 0, 0, 0, None) == 1
+    assert b"seqlen" in lib.fpscan_last_error()
+    assert lib.fpscan_scan_fwd_anylen(16, 24, 16, 1, 1, 7, 0, 0, None) == 1
+    assert b"aligned" in lib.fpscan_last_error()
+    assert lib.fpscan_scan_fwd_anylen(4096, 8192, 8192 + 64, 1, 1, 33, 0, 0, None) == 1
+    assert b"overlap" in lib.fpscan_last_error()
+    rc = lib.fpscan_scan_bwd_anylen(4096, 1 << 20, 2 << 20, 4096 + 16, 3 << 20, 1, 1, 33, 0, None)
+    assert rc == 1 and b"overlap" in lib.fpscan_last_error()
+    assert lib.fpscan_scan_fwd_anylen(0, 0, 0, 0, 4, 1000, 0, 0, None) == 0
+    assert lib.fpscan_scan_bwd_anylen(0, 0, 0, 0, 0, 3, 0, 7, 2, None) == 0
