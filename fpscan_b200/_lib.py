@@ -30,6 +30,10 @@ SIGNATURES = {
     "fpscan_scan_bwd_act": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
     "fpscan_scan_fwd_anylen": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp],
     "fpscan_scan_bwd_anylen": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
+    "fpscan_cl_workspace_bytes": [_c_i64, _c_i64, _c_i64, _c_int, _c_int],
+    "fpscan_scan_fwd_cl": [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _vp, _c_i64, _vp],
+    "fpscan_scan_bwd_cl": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp, _c_i64,
+                           _vp],
     "fpscan_scan_bwd": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_fwd_reduce": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_fwd_scan": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
@@ -67,7 +71,8 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = argtypes
             fn.restype = {"fpscan_last_error": ctypes.c_char_p,
-                          "fpscan_scan_fwd_workspace_bytes": ctypes.c_int64}.get(name, ctypes.c_int)
+                          "fpscan_scan_fwd_workspace_bytes": ctypes.c_int64,
+                          "fpscan_cl_workspace_bytes": ctypes.c_int64}.get(name, ctypes.c_int)
         ver = lib.fpscan_abi_version()
         if ver != EXPECTED_ABI_VERSION:
             raise ImportError(f"libfpscan_b200 ABI version {ver}, expected {EXPECTED_ABI_VERSION}")

@@ -506,3 +506,114 @@ int fpscan_scan_bwd_anylen(const void* gates, const void* y, const void* grad_ou
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ channel-last
+static int check_cl(int64_t batch, int64_t seqlen, int64_t dim, int dtype) {
+  FPSCAN_TRY(check_dtype(dtype));
+  if (batch < 0 || dim < 0 || seqlen < 1)
+    return fail(FPSCAN_ERR_INVALID,
+                "batch (%lld) and dim (%lld) must be non-negative and seqlen (%lld) >= 1",
+                (long long)batch, (long long)dim, (long long)seqlen);
+  if ((dim * dtype_size(dtype)) % 16 != 0)
+    return fail(FPSCAN_ERR_INVALID,
+                "dim (%lld) must be a multiple of %d for this dtype (16-byte rows)", (long long)dim,
+                16 / dtype_size(dtype));
+  if (batch >= (int64_t(1) << 31) || seqlen >= (int64_t(1) << 31) - 64 ||
+      dim >= (int64_t(1) << 31))
+    return fail(FPSCAN_ERR_INVALID, "batch, seqlen and dim must each be below 2^31");
+  if (batch != 0 && dim != 0 && batch * seqlen > INT64_MAX / dim / 8)
+    return fail(FPSCAN_ERR_INVALID, "tensor too large");
+  return FPSCAN_OK;
+}
+
+extern "C" {
+
+int64_t fpscan_cl_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim, int dtype,
+                                  int backward) {
+  if (check_cl(batch, seqlen, dim, dtype) != FPSCAN_OK) return 0;
+  return cl_workspace_bytes(batch, seqlen, dim, dtype, backward != 0);
+}
+
+int fpscan_scan_fwd_cl(const void* gates, const void* tokens, void* out, int64_t batch,
+                       int64_t seqlen, int64_t dim, int dtype, int reverse, void* workspace,
+                       int64_t workspace_bytes, void* stream) {
+  FPSCAN_TRY(check_cl(batch, seqlen, dim, dtype));
+  if (batch == 0 || dim == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(tokens, "tokens"));
+  FPSCAN_TRY(check_ptr(out, "out"));
+  FPSCAN_TRY(check_ptr(workspace, "workspace"));
+  const int64_t need = cl_workspace_bytes(batch, seqlen, dim, dtype, false);
+  if (workspace_bytes < need)
+    return fail(FPSCAN_ERR_INVALID, "workspace too small: %lld bytes, need %lld",
+                (long long)workspace_bytes, (long long)need);
+  const uintptr_t bytes = (uintptr_t)(batch * seqlen * dim * dtype_size(dtype));
+  const Span so{"out", (uintptr_t)out, (uintptr_t)out + bytes};
+  const Span sg{"gates", (uintptr_t)gates, (uintptr_t)gates + bytes};
+  const Span st{"tokens", (uintptr_t)tokens, (uintptr_t)tokens + bytes};
+  const Span sw{"workspace", (uintptr_t)workspace, (uintptr_t)workspace + (uintptr_t)need};
+  for (const Span* in : {&sg, &st})
+    if (overlaps(so, *in) && so.lo != in->lo)
+      return fail(FPSCAN_ERR_INVALID, "out partially overlaps %s", in->name);
+  for (const Span* t : {&so, &sg, &st})
+    if (overlaps(sw, *t)) return fail(FPSCAN_ERR_INVALID, "workspace overlaps %s", t->name);
+  ClArgs a{};
+  a.gates = gates;
+  a.tokens = tokens;
+  a.out = out;
+  a.workspace = workspace;
+  a.workspace_bytes = (uint64_t)workspace_bytes;
+  a.batch = batch;
+  a.seqlen = seqlen;
+  a.dim = dim;
+  a.dtype = dtype;
+  a.reverse = reverse ? 1 : 0;
+  a.backward = 0;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return cuda_result(launch_cl(a), "fpscan_scan_fwd_cl launch");
+}
+
+int fpscan_scan_bwd_cl(const void* gates, const void* y, const void* grad_out, void* dgates,
+                       void* dtokens, int64_t batch, int64_t seqlen, int64_t dim, int dtype,
+                       void* workspace, int64_t workspace_bytes, void* stream) {
+  FPSCAN_TRY(check_cl(batch, seqlen, dim, dtype));
+  if (batch == 0 || dim == 0) return ok();
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(y, "y"));
+  FPSCAN_TRY(check_ptr(grad_out, "grad_out"));
+  FPSCAN_TRY(check_ptr(dgates, "dgates"));
+  FPSCAN_TRY(check_ptr(dtokens, "dtokens"));
+  FPSCAN_TRY(check_ptr(workspace, "workspace"));
+  const int64_t need = cl_workspace_bytes(batch, seqlen, dim, dtype, true);
+  if (workspace_bytes < need)
+    return fail(FPSCAN_ERR_INVALID, "workspace too small: %lld bytes, need %lld",
+                (long long)workspace_bytes, (long long)need);
+  const uintptr_t bytes = (uintptr_t)(batch * seqlen * dim * dtype_size(dtype));
+  const Span all[6] = {{"gates", (uintptr_t)gates, (uintptr_t)gates + bytes},
+                       {"y", (uintptr_t)y, (uintptr_t)y + bytes},
+                       {"grad_out", (uintptr_t)grad_out, (uintptr_t)grad_out + bytes},
+                       {"workspace", (uintptr_t)workspace, (uintptr_t)workspace + (uintptr_t)need},
+                       {"dgates", (uintptr_t)dgates, (uintptr_t)dgates + bytes},
+                       {"dtokens", (uintptr_t)dtokens, (uintptr_t)dtokens + bytes}};
+  for (int i = 3; i < 6; ++i)
+    for (int j = 0; j < i; ++j)
+      if (overlaps(all[i], all[j]))
+        return fail(FPSCAN_ERR_INVALID, "%s overlaps %s", all[i].name, all[j].name);
+  ClArgs a{};
+  a.gates = gates;
+  a.y = y;
+  a.grad_out = grad_out;
+  a.dgates = dgates;
+  a.dtokens = dtokens;
+  a.workspace = workspace;
+  a.workspace_bytes = (uint64_t)workspace_bytes;
+  a.batch = batch;
+  a.seqlen = seqlen;
+  a.dim = dim;
+  a.dtype = dtype;
+  a.backward = 1;
+  a.stream = static_cast<cudaStream_t>(stream);
+  return cuda_result(launch_cl(a), "fpscan_scan_bwd_cl launch");
+}
+
+}  // extern "C"

@@ -25,7 +25,7 @@ constexpr int kWarps = kThreads / 32;
 // Device-side status word.  Bounded waits that give up set a bit here instead
 // of hanging the GPU; the host reads and clears it through
 // fpscan_device_status().
-enum : unsigned { kStatusWaitTimeout = 1u, kStatusLookbackTimeout = 2u };
+enum : unsigned { kStatusWaitTimeout = 1u, kStatusLookbackTimeout = 2u, kStatusMisaligned = 4u };
 
 extern __device__ unsigned int g_status;
 

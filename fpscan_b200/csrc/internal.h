@@ -84,6 +84,26 @@ struct AnyArgs {
   int nv = 1;            // 16-byte vectors per thread per chunk (1 or 2)
 };
 
+// Channel-last (batch, seqlen, dim) scan / backward (scan_cl.cu).
+struct ClArgs {
+  const void* gates;
+  const void* tokens;    // forward
+  void* out;             // forward
+  const void* y;         // backward
+  const void* grad_out;  // backward
+  void* dgates;          // backward
+  void* dtokens;         // backward
+  void* workspace;       // >= cl_workspace_bytes(), 16-byte aligned
+  uint64_t workspace_bytes;
+  int64_t batch;
+  int64_t seqlen;
+  int64_t dim;
+  int dtype;
+  int reverse;
+  int backward;
+  cudaStream_t stream;
+};
+
 // Records `fmt` as this thread's fpscan_last_error() message; returns code.
 int set_error(int code, const char* fmt, ...);
 
@@ -94,6 +114,8 @@ int split_segments(int64_t rows, int64_t seqlen, int dtype, int slots);
 int64_t split_workspace_bytes(int64_t rows, int segments);
 cudaError_t launch_bwd(const BwdArgs& a);
 cudaError_t launch_anylen(const AnyArgs& a);
+cudaError_t launch_cl(const ClArgs& a);
+int64_t cl_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim, int dtype, bool backward);
 cudaError_t launch_carry_combine(const float* gathered, int world, int rank, int64_t rows,
                                  int reverse, float* out, cudaStream_t stream);
 

@@ -23,7 +23,8 @@ import torch
 from . import _lib
 
 __all__ = ["pscan", "scan_forward", "PScan", "pscan_gated", "scan_forward_gated",
-           "pscan_anylen", "scan_forward_anylen"]
+           "pscan_anylen", "scan_forward_anylen", "pscan_channels_last",
+           "scan_forward_channels_last"]
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 MIN_SEQLEN = 32
@@ -86,8 +87,10 @@ def _stream_ptr(device: torch.device) -> int:
 _workspaces: dict = {}
 
 
-def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
-    key = (device.index, stream)
+def _workspace(device: torch.device, stream: int, nbytes: int, kind: str = "split") -> torch.Tensor:
+    # one workspace per kernel family: status words of different families
+    # carry independent epochs and must not share memory
+    key = (device.index, stream, kind)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
@@ -341,3 +344,95 @@ class PScanAnyLen(torch.autograd.Function):
 def pscan_anylen(gates: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
     """Differentiable ``pscan`` for any seqlen >= 1 (e.g. 1000, 3, 200000)."""
     return PScanAnyLen.apply(gates, tokens)
+
+
+# --------------------------------------------------------------------------- channel-last layout
+def validate_channels_last(gates: torch.Tensor, tokens: torch.Tensor,
+                           out: Optional[torch.Tensor] = None) -> None:
+    """Checks for (batch, seqlen, dim) tensors scanned along seqlen."""
+    _check_input(gates, "gates")
+    _check_input(tokens, "tokens")
+    if tokens.dim() != 3:
+        raise RuntimeError(f"tokens must be 3-D (batch, seqlen, dim), got {tuple(tokens.shape)}")
+    if gates.shape != tokens.shape or gates.dtype != tokens.dtype or gates.device != tokens.device:
+        raise RuntimeError("gates and tokens must have the same shape, dtype and device")
+    if tokens.shape[1] < 1:
+        raise RuntimeError(f"seqlen must be >= 1 (got {tokens.shape[1]})")
+    vec = 16 // tokens.element_size()
+    if tokens.shape[2] % vec:
+        raise RuntimeError(f"dim must be a multiple of {vec} for {tokens.dtype} (got {tokens.shape[2]})")
+    if out is not None:
+        if out.shape != tokens.shape or out.dtype != tokens.dtype or out.device != tokens.device:
+            raise RuntimeError("out must match tokens in shape, dtype and device")
+        if not out.is_contiguous():
+            raise RuntimeError("out must be contiguous")
+
+
+def _cl_workspace(t: torch.Tensor, backward: bool):
+    b, l, d = t.shape
+    lib = _lib.load()
+    nbytes = lib.fpscan_cl_workspace_bytes(b, l, d, DTYPE_CODES[t.dtype], 1 if backward else 0)
+    stream = _stream_ptr(t.device)
+    return _workspace(t.device, stream, nbytes, kind="channels_last"), stream
+
+
+def scan_forward_channels_last(gates: torch.Tensor, tokens: torch.Tensor, reverse: bool = False,
+                               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Scan along dim 1 of (batch, seqlen, dim) tensors:
+    y[:, t] = gates[:, t] * y[:, t-1] + tokens[:, t] (zero initial state).
+
+    Replaces the reference's documented channel-last usage
+    ``scan_forward(g.mT.contiguous(), x.mT.contiguous()).mT.contiguous()``
+    (README.md:94-99) without the transposes.  Any seqlen >= 1; dim must be a
+    multiple of 16 bytes' worth of elements."""
+    _lib.load()
+    validate_channels_last(gates, tokens, out)
+    if out is None:
+        out = torch.empty_like(tokens)
+    b, l, d = tokens.shape
+    if b == 0 or d == 0:
+        return out
+    with torch.cuda.device(tokens.device):
+        ws, stream = _cl_workspace(tokens, False)
+        _lib.call("fpscan_scan_fwd_cl", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(), b, l,
+                  d, DTYPE_CODES[tokens.dtype], 1 if reverse else 0, ws.data_ptr(), ws.numel(),
+                  stream)
+    return out
+
+
+def scan_backward_channels_last(gates: torch.Tensor, out: torch.Tensor,
+                                grad_output: torch.Tensor):
+    """Fused backward of ``pscan_channels_last``: (grad_gates, grad_tokens)."""
+    validate_channels_last(gates, grad_output)
+    validate_channels_last(out, grad_output)
+    dgates = torch.empty_like(grad_output)
+    dtokens = torch.empty_like(grad_output)
+    b, l, d = grad_output.shape
+    if b == 0 or d == 0:
+        return dgates, dtokens
+    with torch.cuda.device(grad_output.device):
+        ws, stream = _cl_workspace(grad_output, True)
+        _lib.call("fpscan_scan_bwd_cl", gates.data_ptr(), out.data_ptr(), grad_output.data_ptr(),
+                  dgates.data_ptr(), dtokens.data_ptr(), b, l, d,
+                  DTYPE_CODES[grad_output.dtype], ws.data_ptr(), ws.numel(), stream)
+    return dgates, dtokens
+
+
+class PScanChannelsLast(torch.autograd.Function):
+    """``PScan`` on (batch, seqlen, dim) tensors."""
+
+    @staticmethod
+    def forward(ctx, gates, tokens):
+        out = scan_forward_channels_last(gates, tokens)
+        ctx.save_for_backward(gates, out)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        gates, out = ctx.saved_tensors
+        return scan_backward_channels_last(gates, out, grad_output.contiguous())
+
+
+def pscan_channels_last(gates: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
+    """Differentiable scan along dim 1 of (batch, seqlen, dim) tensors."""
+    return PScanChannelsLast.apply(gates, tokens)

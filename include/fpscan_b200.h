@@ -129,6 +129,34 @@ FPSCAN_API int fpscan_scan_bwd_anylen(const void* gates, const void* y, const vo
                                       int64_t seqlen, int dtype, void* stream);
 
 /*
+ * Channel-last layout: gates, tokens, out are (batch, seqlen, dim) contiguous
+ * and the recurrence runs along seqlen: y[b,t,d] = gates[b,t,d]*y[b,t-1,d] +
+ * tokens[b,t,d], zero initial state (reverse: from t = seqlen-1).  The
+ * reference has no such layout: its README (README.md:94-99) transposes with
+ * .mT.contiguous() around pscan.  Any seqlen >= 1; dim*itemsize must be a
+ * multiple of 16.  Needs a workspace of fpscan_cl_workspace_bytes() bytes
+ * (16-byte aligned, about 3% of one tensor; reused across calls ordered on
+ * one stream without clearing; calls that may overlap need separate
+ * workspaces).  `out` may equal gates or tokens.
+ */
+FPSCAN_API int64_t fpscan_cl_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim,
+                                             int dtype, int backward);
+FPSCAN_API int fpscan_scan_fwd_cl(const void* gates, const void* tokens, void* out,
+                                  int64_t batch, int64_t seqlen, int64_t dim, int dtype,
+                                  int reverse, void* workspace, int64_t workspace_bytes,
+                                  void* stream);
+
+/*
+ * Fused backward (fpscan/ops.py:70-83 semantics) in the channel-last layout:
+ * dtokens[t] = grad_out[t] + gates[t+1]*dtokens[t+1], dgates[t] =
+ * dtokens[t]*y[t-1], along seqlen.  Outputs must not overlap anything.
+ */
+FPSCAN_API int fpscan_scan_bwd_cl(const void* gates, const void* y, const void* grad_out,
+                                  void* dgates, void* dtokens, int64_t batch, int64_t seqlen,
+                                  int64_t dim, int dtype, void* workspace,
+                                  int64_t workspace_bytes, void* stream);
+
+/*
  * Scan with a per-row initial state `init` (fp32, batch*dim values):
  * y[0] = gates[0]*init + tokens[0] (reverse: y[L-1] = gates[L-1]*init +
  * tokens[L-1]).  The final state is the last element of out in scan order.
@@ -208,8 +236,10 @@ FPSCAN_API const char* fpscan_last_error(void);
 
 /* Synchronously read (and if `clear`, reset) the current device's status
  * word.  Bit 0: a kernel gave up a bounded wait on its own copies; bit 1: a
- * split-row scan gave up waiting for a preceding segment.  Results of such a
- * launch are not valid.  0 = healthy. */
+ * split-row or channel-last scan gave up waiting for a preceding segment;
+ * bit 2: a channel-last tile found its shared-memory staging buffer
+ * misaligned for TMA and skipped it.  Results of such a launch are not
+ * valid.  0 = healthy. */
 FPSCAN_API int fpscan_device_status(unsigned* status, int clear);
 
 #ifdef __cplusplus

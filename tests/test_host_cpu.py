@@ -146,3 +146,29 @@ def test_anylen_validation_and_c_abi_checks():
     assert rc == 1 and b"overlap" in lib.fpscan_last_error()
     assert lib.fpscan_scan_fwd_anylen(0, 0, 0, 0, 4, 1000, 0, 0, None) == 0
     assert lib.fpscan_scan_bwd_anylen(0, 0, 0, 0, 0, 3, 0, 7, 2, None) == 0
+
+
+def test_channels_last_validation_and_c_abi_checks():
+    t = torch.empty(2, 10, 64)
+    lib = _lib.load()
+    # dim*itemsize must be a multiple of 16
+    assert lib.fpscan_scan_fwd_cl(16, 16, 16, 1, 10, 6, 0, 0, 16, 1 << 20, None) == 1
+    assert b"multiple" in lib.fpscan_last_error()
+    assert lib.fpscan_scan_fwd_cl(16, 16, 16, 1, 0, 8, 0, 0, 16, 1 << 20, None) == 1
+    assert b"seqlen" in lib.fpscan_last_error()
+    need = lib.fpscan_cl_workspace_bytes(2, 1000, 256, 2, 0)
+    # tiles = 2 batches * 1 column block * ceil(1000 / 64) segments, 3088-byte records
+    assert need == 256 + 2 * 1 * 16 * 3088
+    assert lib.fpscan_cl_workspace_bytes(2, 1000, 256, 2, 1) == 256 + 2 * 32 * 3088
+    assert lib.fpscan_scan_fwd_cl(1 << 20, 2 << 20, 3 << 20, 2, 1000, 256, 2, 0, 4 << 20, need - 16,
+                                  None) == 1
+    assert b"workspace too small" in lib.fpscan_last_error()
+    assert lib.fpscan_scan_fwd_cl(1 << 20, 2 << 20, 3 << 20, 2, 1000, 256, 2, 0, (3 << 20) + 64,
+                                  need, None) == 1
+    assert b"overlap" in lib.fpscan_last_error()
+    rc = lib.fpscan_scan_bwd_cl(1 << 20, 2 << 20, 3 << 20, (1 << 20) + 16, 5 << 20, 2, 10, 256, 2,
+                                6 << 20, 1 << 20, None)
+    assert rc == 1 and b"overlap" in lib.fpscan_last_error()
+    assert lib.fpscan_scan_fwd_cl(0, 0, 0, 0, 10, 256, 2, 0, 0, 0, None) == 0
+    with pytest.raises(RuntimeError):
+        ops.validate_channels_last(t, t)  # CPU tensors are rejected like the reference's
