@@ -118,3 +118,44 @@ def test_channels_last_in_place_repeat_and_errors():
         fpscan.scan_forward_channels_last(g[:, :, :63].contiguous(), x[:, :, :63].contiguous())
     with pytest.raises(RuntimeError):
         fpscan.scan_forward_channels_last(g.transpose(1, 2), x.transpose(1, 2))
+
+
+_PATH_SCRIPT = r"""
+import sys, numpy as np, torch
+sys.path.insert(0, {repo!r}); sys.path.insert(0, {tests!r})
+import fpscan_b200 as fpscan, oracle
+from test_channels_last_gpu import _inputs, _t64, _from64, _vec
+from test_scan_gpu import _check
+for dtype in (torch.float32, torch.bfloat16, torch.float16):
+    for (b, l, nv) in [(2, 1000, 32), (3, 333, 17), (1, 7, 9), (2, 4100, 64), (8, 300, 130)]:
+        shape = (b, l, nv * _vec(dtype))
+        g, x, go = _inputs(shape, dtype, seed=l + nv)
+        g64, x64 = _t64(g), _t64(x)
+        for rev in (False, True):
+            _check(fpscan.scan_forward_channels_last(g, x, reverse=rev),
+                   _from64(oracle.scan_f64(g64, x64, rev)), dtype, "fwd")
+        gg, xx = g.clone().requires_grad_(), x.clone().requires_grad_()
+        dg, dt = torch.autograd.grad(fpscan.pscan_channels_last(gg, xx), (gg, xx), go)
+        dg64, dt64 = oracle.scan_bwd_f64(g64, oracle.scan_f64(g64, x64), _t64(go))
+        _check(dt, _from64(dt64), dtype, "dtokens")
+        _check(dg, _from64(dg64), dtype, "dgates")
+from fpscan_b200 import _lib
+assert _lib.device_status() == 0
+print("ok")
+"""
+
+
+@pytest.mark.parametrize("path", ["stream", "lookback"])
+def test_channels_last_both_kernels(path):
+    """The streaming (one CTA per column) and look-back (columns split in
+    time) kernels, each forced on the same cases in a fresh process (the
+    choice is read once per process)."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = _PATH_SCRIPT.format(repo=os.path.dirname(here), tests=here)
+    env = dict(os.environ, FPSCAN_B200_CL_PATH=path)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]

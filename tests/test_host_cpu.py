@@ -157,8 +157,9 @@ def test_channels_last_validation_and_c_abi_checks():
     assert lib.fpscan_scan_fwd_cl(16, 16, 16, 1, 0, 8, 0, 0, 16, 1 << 20, None) == 1
     assert b"seqlen" in lib.fpscan_last_error()
     need = lib.fpscan_cl_workspace_bytes(2, 1000, 256, 2, 0)
-    # tiles = 2 batches * 1 column block * ceil(1000 / 64) segments, 3088-byte records
-    assert need == 256 + 2 * 1 * 16 * 3088
+    # tiles = 2 batches * 1 column block * ceil(1000 / 32) segments (32 timesteps
+    # per tile by default), 3088-byte records
+    assert need == 256 + 2 * 1 * 32 * 3088
     assert lib.fpscan_cl_workspace_bytes(2, 1000, 256, 2, 1) == 256 + 2 * 32 * 3088
     assert lib.fpscan_scan_fwd_cl(1 << 20, 2 << 20, 3 << 20, 2, 1000, 256, 2, 0, 4 << 20, need - 16,
                                   None) == 1
