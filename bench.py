@@ -12,6 +12,7 @@ larger than L2 (126 MB), so no flush is needed between steps.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME]
     python bench.py --impl reference     # the reference's CPU path, timed on the host
+    python bench.py --config anylen | channels_last --steps 20   # per-kernel tables
 
 Prints one JSON line (rank 0).
 """
@@ -47,12 +48,22 @@ CONFIGS = {
     # exp(-softplus(z)) on load; the backward writes dz
     "shard_bd_gated": dict(batch=16, dim=5120, seqlen=16384, dtype="bfloat16",
                            gates="logits", tokens_scale="unit"),
+    # the same at config-3 size (small enough for a full ncu capture)
+    "halfbwd_gated": dict(batch=8, dim=2048, seqlen=8192, dtype="bfloat16", gates="logits",
+                          tokens_scale="unit"),
     # sequence-sharded fp32 fwd+bwd, seqlen split over the ranks
     "shard_seq": dict(batch=4, dim=8192, seqlen=65536, dtype="float32", gates="0.999+0.001U",
                       tokens_scale="1/L"),
     # forward-only sweep, fp32, batch 2 x dim 256, seqlen 32..65536
     "fwd_sweep": dict(batch=2, dim=256, seqlen=65536, dtype="float32", gates="0.99+0.01U",
                       tokens_scale="1/L"),
+    # beyond the reference (one GPU, per-kernel tables): any seqlen, and the
+    # channel-last (batch, seqlen, dim) layout
+    "anylen": dict(shapes=[(8, 2048, 8191, "bfloat16"), (16, 5120, 16383, "bfloat16"),
+                           (8, 2048, 8191, "float32"), (2, 256, 100000, "float32")]),
+    "channels_last": dict(shapes=[(8, 8192, 2048, "bfloat16"), (16, 16384, 5120, "bfloat16"),
+                                  (8, 8192, 2048, "float32"), (4, 65536, 8192, "float32"),
+                                  (2, 65536, 256, "float32"), (1, 100000, 512, "bfloat16")]),
 }
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the backward
@@ -580,6 +591,88 @@ def run_fwd_sweep(args, cfg):
         "sweep": table}), flush=True)
 
 
+def run_layout_table(args, kind):
+    """One GPU: forward, reverse and fused-backward GB/s (algorithmic bytes:
+    3*N*s and 5*N*s) of the any-seqlen or channel-last kernels at fixed
+    shapes, CUDA events over K calls after W warm-up calls (every tensor is
+    larger than L2 except the few-channel rows, noted in the table).  For the
+    channel-last layout the reference's own recipe (transpose, last-axis
+    scan, transpose back; here on this package's kernels) is timed beside it
+    where the seqlen is one the reference accepts.  `value` = first row's
+    forward+backward GB/s."""
+    import fpscan_b200
+    from fpscan_b200 import _lib, ops
+
+    world, rank, local = _dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    _lib.load()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / args.steps
+
+    table = []
+    for (d0, d1, d2, dt) in CONFIGS[kind]["shapes"][:args.max_shapes]:
+        dtype = getattr(torch, dt)
+        gen = torch.Generator(device=device).manual_seed(d0 + d1 + d2)
+        shape = (d0, d1, d2)
+        g = (0.9 + 0.1 * torch.rand(shape, generator=gen, device=device)).to(dtype)
+        x = torch.randn(shape, generator=gen, device=device).to(dtype)
+        go = torch.randn(shape, generator=gen, device=device).to(dtype)
+        y = torch.empty_like(x)
+        n, s = x.numel(), x.element_size()
+        if kind == "anylen":
+            fwd = lambda rev=False: fpscan_b200.scan_forward_anylen(g, x, reverse=rev, out=y)  # noqa: E731
+            bwd = lambda: ops.scan_backward_anylen(g, y, go)  # noqa: E731
+            layout = "(batch, dim, seqlen)"
+        else:
+            fwd = lambda rev=False: fpscan_b200.scan_forward_channels_last(g, x, reverse=rev, out=y)  # noqa: E731
+            bwd = lambda: ops.scan_backward_channels_last(g, y, go)  # noqa: E731
+            layout = "(batch, seqlen, dim)"
+        ms_f, ms_r = timed(lambda: fwd()), timed(lambda: fwd(True))
+        fwd()
+        ms_b = timed(bwd)
+        row = {"shape": list(shape), "layout": layout, "dtype": dt,
+               "fwd_gbs": round(3 * n * s / ms_f / 1e6, 1), "rev_gbs": round(3 * n * s / ms_r / 1e6, 1),
+               "bwd_gbs": round(5 * n * s / ms_b / 1e6, 1), "fwd_ms": round(ms_f, 4),
+               "bwd_ms": round(ms_b, 4), "fwd_bwd_gbs": round(8 * n * s / (ms_f + ms_b) / 1e6, 1),
+               "larger_than_l2": 3 * n * s > 126e6}
+        if kind == "channels_last":
+            row["kernel"] = ("streaming" if fpscan_b200.ops._lib.load().fpscan_cl_workspace_bytes(
+                d0, d1, d2, ops.DTYPE_CODES[dtype], 0) <= 256 else "look-back")
+            if d1 & (d1 - 1) == 0 and 32 <= d1 <= 65536 and 3 * n * s < 20e9:
+                def recipe():
+                    return fpscan_b200.scan_forward(g.mT.contiguous(), x.mT.contiguous()).mT.contiguous()
+                row["reference_recipe_fwd_ms"] = round(timed(recipe), 4)
+        table.append(row)
+        del g, x, go, y
+        torch.cuda.empty_cache()
+    peak, peak_kind = _peaks()
+    first = table[0]
+    print(json.dumps({
+        "metric": METRIC, "value": first["fwd_bwd_gbs"], "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(first["fwd_ms"] + first["bwd_ms"], 4), "higher_is_better": True,
+        "scaling": "none", "vs_baseline": None, "dtype": first["dtype"],
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"{kind}: forward / reverse / fused backward per shape",
+                   "l2": "inputs larger than L2 except where larger_than_l2 is false"},
+        "pct_of_hbm_peak": round(100 * first["fwd_bwd_gbs"] / peak, 2), "peak_source": peak_kind,
+        "table": table, "device_status": _lib.device_status()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -590,15 +683,20 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--max-shapes", type=int, default=None,
+                    help="anylen / channels_last: only the first N shapes of the table")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
-        run_reference(args, cfg)
+        # the reference's CPU path exists for the last-axis scan only
+        run_reference(args, cfg if "dtype" in cfg else CONFIGS["shard_bd"])
     elif args.config == "shard_seq":
         run_shard_seq(args, cfg)
     elif args.config == "fwd_sweep":
         run_fwd_sweep(args, cfg)
+    elif args.config in ("anylen", "channels_last"):
+        run_layout_table(args, args.config)
     else:
         run_fpscan(args, cfg)
 

@@ -138,14 +138,15 @@ int tuned_nv(bool forward, int dtype) {
   return forward ? 1 : 2;
 }
 
-// Gated kernels (activation fused), 16-bit types, measured at BASELINE
-// config 4: the forward does more work per element and runs faster with two
-// vectors per thread (5.7 vs 5.2 TB/s); the backward spills at two vectors
-// per thread under its register budget and runs with one (5.1 vs 3.2 TB/s).
+// Gated kernels (activation fused), measured at BASELINE config 4 (bf16):
+// two vectors per thread in both directions -- the forward does more work
+// per element (5.75 TB/s vs 5.2 with one), the backward runs under a 2-CTA
+// register budget (5.6 TB/s; one vector: 5.1; two at the 3-CTA budget
+// spilled: 3.2).
 int tuned_nv_act(bool forward, int dtype, int act) {
   if (act == kActNone || dtype == FPSCAN_F32 || getenv("FPSCAN_B200_NV"))
     return tuned_nv(forward, dtype);
-  return forward ? 2 : 1;
+  return 2;
 }
 
 constexpr int64_t kRefMinL = 32, kRefMaxL = 65536;  // csrc/full_scan/full_scan.cu:207-233
@@ -498,9 +499,9 @@ int fpscan_scan_bwd_anylen(const void* gates, const void* y, const void* grad_ou
   a.backward = 1;
   a.num_sms = num_sms_current();
   a.stream = static_cast<cudaStream_t>(stream);
-  // fp32: two vectors per thread (6.3-6.4 TB/s vs 5.3); 16-bit types: one
-  // (two spill under the register budget: 3.8 vs 5.0 TB/s)
-  a.nv = dtype == FPSCAN_F32 ? 2 : 1;
+  // two vectors per thread (fp32 6.3 TB/s vs 5.3; bf16, at a 2-CTA register
+  // budget, 5.2-5.6 vs 5.0 with one)
+  a.nv = 2;
   if (const char* v = getenv("FPSCAN_B200_ANY_BWD_NV")) a.nv = v[0] == '2' ? 2 : 1;
   return cuda_result(launch_anylen(a), "fpscan_scan_bwd_anylen launch");
 }

@@ -35,6 +35,9 @@ template <typename T, int NV>
 struct AnyCfg {
   static constexpr int kStages = NV == 1 ? 4 : 3;
   static constexpr int kMinBlocks = 3;
+  // the backward with two vectors per thread gets a 2-CTA register budget
+  // (it spills under the 3-CTA one)
+  static constexpr int kBwdMinBlocks = NV == 2 ? 2 : 3;
   static constexpr int SV = kThreads * NV;  // 16-byte vectors per chunk
   static constexpr int fwd_smem() { return kStages * 2 * SV * 16; }
   static constexpr int kBwdStages = NV == 1 ? 4 : 3;
@@ -373,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, (AnyCfg<T, NV>::kMinBlocks))
 // at a thread's edges come from one extra staged vector after the gates chunk
 // and before the y chunk.
 template <typename T, int NV>
-__global__ void __launch_bounds__(kThreads, (AnyCfg<T, NV>::kMinBlocks))
+__global__ void __launch_bounds__(kThreads, (AnyCfg<T, NV>::kBwdMinBlocks))
     scan_anylen_bwd_kernel(const AnyKParams p) {
   constexpr int V = Elem<T>::kVec;
   constexpr int E = V * NV;

@@ -51,7 +51,10 @@ struct BwdKParams {
 };
 
 template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY, int ACT>
-__global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks) scan_bwd_kernel(const BwdKParams p) {
+// Gated variants with two vectors per thread hold more live values: they get
+// a 2-CTA register budget (128) instead of spilling under the 3-CTA one.
+__global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : BwdCfg<NV>::kMinBlocks)
+    scan_bwd_kernel(const BwdKParams p) {
   constexpr int V = Elem<T>::kVec;
   constexpr int E = V * NV;
   constexpr int CH = kThreads * E;

@@ -525,12 +525,13 @@ __global__ void __launch_bounds__(kClThreads, 1) scan_cl_kernel(const __grid_con
 // Reading whole 128-byte rows per 8 lanes is bank-conflict free.
 constexpr int kStreamVecs = 8;
 constexpr int kStreamRowBytes = kStreamVecs * 16;
-constexpr int kStreamGroups = kThreads / kStreamVecs;  // 32 thread groups
 
-template <typename T, int MODE, int TW, int S>
+template <typename T, int MODE, int TW, int S, int NTH>
 struct StreamCfg {
+  static constexpr int NW = NTH / 32;          // warps
+  static constexpr int NG = NTH / kStreamVecs;  // thread groups
   static constexpr int kTiles = MODE == kClBwd ? 3 : 2;
-  static constexpr int R = kStreamGroups * TW;  // timesteps per chunk
+  static constexpr int R = NG * TW;  // timesteps per chunk
   static constexpr int kTileBytes = R * kStreamRowBytes;
   static constexpr int kStageBytes = kTiles * kTileBytes;
   static constexpr int smem() { return S * kStageBytes + 128; }  // + TMA alignment slack
@@ -545,10 +546,11 @@ struct StreamParams {
   int64_t cb;    // column blocks per batch (ceil(dv / 8))
 };
 
-template <typename T, int MODE, int TW, int S>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename T, int MODE, int TW, int S, int NTH>
+__global__ void __launch_bounds__(NTH, 1)
     scan_cl_stream_kernel(const __grid_constant__ StreamParams p) {
-  using Cfg = StreamCfg<T, MODE, TW, S>;
+  using Cfg = StreamCfg<T, MODE, TW, S, NTH>;
+  constexpr int NW = Cfg::NW;
   constexpr int V = Elem<T>::kVec;
   constexpr int R = Cfg::R;
   constexpr bool DESC = MODE != kClFwd;
@@ -558,7 +560,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* csm = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(csm_raw) + 127) & ~uintptr_t(127));
   __shared__ __align__(8) uint64_t s_bar[S];
-  __shared__ float2 s_wt[2][kWarps][kStreamVecs][V];  // warp maps per vector, by chunk parity
+  // warp maps per channel and vector (vectors innermost: conflict-free), by chunk parity
+  __shared__ float2 s_wt[2][NW][V][kStreamVecs];
   __shared__ float s_carry[2][kStreamVecs][V];          // state after a chunk, by chunk parity
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -666,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int buf = (int)(k & 1);
     if (grp == 32 / kStreamVecs - 1)
 #pragma unroll
-      for (int c = 0; c < V; ++c) s_wt[buf][warp][vec][c] = make_float2(A[c], B[c]);
+      for (int c = 0; c < V; ++c) s_wt[buf][warp][c][vec] = make_float2(A[c], B[c]);
 
     if (__syncthreads_or(!ok)) {
       aborted = true;
@@ -693,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int q = 0; q < warp; ++q) {
 #pragma unroll
       for (int c = 0; c < V; ++c) {
-        const float2 mq = s_wt[buf][q][vec][c];
+        const float2 mq = s_wt[buf][q][c][vec];
         st[c] = zero ? mq.y : fmaf(mq.x, st[c], mq.y);
       }
       zero = false;
@@ -725,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     // the chunk's last timestep (processing order) carries into the next
-    if (tg == kStreamGroups - 1)
+    if (tg == Cfg::NG - 1)
 #pragma unroll
       for (int c = 0; c < V; ++c) s_carry[buf][vec][c] = st[c];
 
@@ -865,12 +868,12 @@ cudaError_t launch_cl_mode(const ClArgs& a) {
   }
 }
 
-template <typename T, int MODE, int TW, int S>
+template <typename T, int MODE, int TW, int S, int NTH = kThreads>
 cudaError_t launch_stream_t(const ClArgs& a) {
-  using Cfg = StreamCfg<T, MODE, TW, S>;
+  using Cfg = StreamCfg<T, MODE, TW, S, NTH>;
   constexpr int V = Elem<T>::kVec;
   constexpr int smem = Cfg::smem();
-  auto kern = scan_cl_stream_kernel<T, MODE, TW, S>;
+  auto kern = scan_cl_stream_kernel<T, MODE, TW, S, NTH>;
   static int configured[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -901,14 +904,15 @@ cudaError_t launch_stream_t(const ClArgs& a) {
   }
   if (e != cudaSuccess) return e;
   const int64_t cols = a.batch * p.cb;
-  kern<<<(unsigned)cols, kThreads, smem, a.stream>>>(p);
+  kern<<<(unsigned)cols, NTH, smem, a.stream>>>(p);
   return cudaGetLastError();
 }
 
-// Streaming-kernel shape: TW timesteps per thread group and S ring stages
-// (TW x S).  Defaults: forward 8x3 (192 KiB of stages), backward 8x2 (its
-// three operands leave room for two).  FPSCAN_B200_CL_STREAM=4x4 / 4x3 /
-// 8x2 / 8x3 overrides (8x3 applies to the forward only).
+// Streaming-kernel shape: TW timesteps per thread group, S ring stages and
+// threads per CTA.  Defaults: forward 8x3 (192 KiB of stages), backward 8x2
+// (its three operands leave room for two), 256 threads.
+// FPSCAN_B200_CL_STREAM=4x4 / 4x3 / 8x2 / 8x3 / w4x3 / w4x2 overrides
+// ("w": 512 threads; 8x3 and w4x3 apply to the forward only).
 template <typename T, int MODE>
 cudaError_t launch_stream_mode(const ClArgs& a) {
   static const int cfg = [] {
@@ -918,8 +922,11 @@ cudaError_t launch_stream_mode(const ClArgs& a) {
     if (!strcmp(v, "8x3")) return 2;
     if (!strcmp(v, "4x3")) return 3;
     if (!strcmp(v, "8x2")) return 4;
+    if (!strcmp(v, "w4x3")) return 5;
+    if (!strcmp(v, "w4x2")) return 6;
     return 0;
   }();
+  constexpr bool kBwd = MODE == kClBwd;
   switch (cfg) {
     case 1:
       return launch_stream_t<T, MODE, 4, 4>(a);
@@ -927,8 +934,13 @@ cudaError_t launch_stream_mode(const ClArgs& a) {
       return launch_stream_t<T, MODE, 4, 3>(a);
     case 4:
       return launch_stream_t<T, MODE, 8, 2>(a);
+    case 5:
+      if constexpr (!kBwd) return launch_stream_t<T, MODE, 4, 3, 512>(a);
+      [[fallthrough]];
+    case 6:
+      return launch_stream_t<T, MODE, 4, 2, 512>(a);
     default:
-      if constexpr (MODE == kClBwd) return launch_stream_t<T, MODE, 8, 2>(a);
+      if constexpr (kBwd) return launch_stream_t<T, MODE, 8, 2>(a);
       else return launch_stream_t<T, MODE, 8, 3>(a);
   }
 }
