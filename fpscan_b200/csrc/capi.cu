@@ -204,6 +204,12 @@ static int scan_fwd_impl(const void* gates, const void* tokens, void* out, int64
   FwdArgs a{gates, tokens, out, nullptr, nullptr, nullptr, rows, seqlen, dtype,
             reverse ? 1 : 0, num_sms_current(), static_cast<cudaStream_t>(stream)};
   a.nv = tuned_nv_act(true, dtype, act);
+  // One vector per thread (8-deep ring, 3 CTAs/SM) is the fp32 choice when
+  // rows fill several waves (config 5: 32768 rows); with few rows (config 2:
+  // 512 rows) one row per CTA at 4 CTAs/SM is faster: two vectors per thread.
+  if (act == kActNone && !getenv("FPSCAN_B200_NV") && dtype == FPSCAN_F32 &&
+      rows <= 4 * (int64_t)a.num_sms)
+    a.nv = 2;
   a.act = act;
   return cuda_result(launch_fwd(a), "fpscan_scan_fwd launch");
 }

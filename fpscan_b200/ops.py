@@ -82,6 +82,56 @@ def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+# ---- launch path.  A call's host cost is on the critical path whenever the
+# GPU waits for it (small tensors, back-to-back calls), so the common case
+# avoids torch.cuda.device / Stream objects: the raw current stream and the
+# current device come from torch's C bindings, the device is switched only
+# when the tensors live elsewhere, and ctypes functions are looked up once.
+_get_device = getattr(torch._C, "_cuda_getDevice", None) or torch.cuda.current_device
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None) or \
+    (lambda idx: torch.cuda.current_stream(idx).cuda_stream)
+_fns: dict = {}
+
+
+def _fn(name: str):
+    f = _fns.get(name)
+    if f is None:
+        f = _fns[name] = getattr(_lib.load(), name)
+    return f
+
+
+def _launch(dev: int, name: str, *args) -> None:
+    """Call C-ABI entry point `name`(*args, stream) on device `dev` (its
+    current stream); raise RuntimeError with the library's message on error."""
+    f = _fns.get(name) or _fn(name)
+    prev = _get_device()
+    if prev == dev:
+        rc = f(*args, _raw_stream(dev))
+    else:
+        torch.cuda.set_device(dev)
+        try:
+            rc = f(*args, _raw_stream(dev))
+        finally:
+            torch.cuda.set_device(prev)
+    if rc:
+        _lib.check(rc, name)
+
+
+def _fast_valid(gates: torch.Tensor, tokens: torch.Tensor) -> bool:
+    """True when (gates, tokens) certainly pass validate(); otherwise the
+    caller runs validate() for the precise error."""
+    try:
+        if not (tokens.is_cuda and gates.is_cuda and tokens.dtype is gates.dtype
+                and tokens.dtype in DTYPE_CODES and tokens.dim() == 3
+                and gates.shape == tokens.shape and gates.device == tokens.device
+                and tokens.is_contiguous() and gates.is_contiguous()):
+            return False
+    except AttributeError:
+        return False
+    seqlen = tokens.shape[2]
+    return MIN_SEQLEN <= seqlen <= MAX_SEQLEN and not seqlen & (seqlen - 1)
+
+
 # Split-row workspaces, one per (device, stream): calls ordered on one stream
 # may share one; it is zeroed once when (re)allocated.
 _workspaces: dict = {}
@@ -98,28 +148,38 @@ def _workspace(device: torch.device, stream: int, nbytes: int, kind: str = "spli
     return ws
 
 
+# workspace bytes of the split-row path, per (rows, seqlen, dtype, device)
+_ws_need: dict = {}
+
+
 def fullscan_forward(gates: torch.Tensor, tokens: torch.Tensor, out: torch.Tensor,
                      reverse: bool) -> torch.Tensor:
     """Same contract as the reference extension's ``fullscan_forward``
     (csrc/main.cpp:10 -> warpscan_fwd): validates, scans into ``out``, returns it.
     Few-channel, long-sequence shapes go to the split-row kernel, which needs
     a small per-stream workspace (kept here)."""
-    validate(gates, tokens, out)
+    if not (_fast_valid(gates, tokens) and out.shape == tokens.shape
+            and out.dtype is tokens.dtype and out.device == tokens.device and out.is_contiguous()):
+        validate(gates, tokens, out)
     b, d, l = tokens.shape
-    lib = _lib.load()
     code = DTYPE_CODES[tokens.dtype]
-    with torch.cuda.device(tokens.device):
-        stream = _stream_ptr(tokens.device)
-        ws_bytes = lib.fpscan_scan_fwd_workspace_bytes(b, d, l, code)
-        if ws_bytes > 0:
-            ws = _workspace(tokens.device, stream, ws_bytes)
-            _lib.check(lib.fpscan_scan_fwd_ws(gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
-                                              b, d, l, code, 1 if reverse else 0, ws.data_ptr(),
-                                              ws.numel(), stream), "fpscan_scan_fwd_ws")
-        else:
-            _lib.check(lib.fpscan_scan_fwd(gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
-                                           b, d, l, code, 1 if reverse else 0, stream),
-                       "fpscan_scan_fwd")
+    dev = tokens.get_device()
+    key = (b * d, l, code, dev)
+    ws_bytes = _ws_need.get(key)
+    if ws_bytes is None:
+        prev = _get_device()
+        torch.cuda.set_device(dev)
+        try:
+            ws_bytes = _ws_need[key] = _lib.load().fpscan_scan_fwd_workspace_bytes(b, d, l, code)
+        finally:
+            torch.cuda.set_device(prev)
+    if ws_bytes > 0:
+        ws = _workspace(tokens.device, _raw_stream(dev), ws_bytes)
+        _launch(dev, "fpscan_scan_fwd_ws", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
+                b, d, l, code, 1 if reverse else 0, ws.data_ptr(), ws.numel())
+    else:
+        _launch(dev, "fpscan_scan_fwd", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
+                b, d, l, code, 1 if reverse else 0)
     return out
 
 
@@ -145,7 +205,8 @@ def scan_forward(gates: torch.Tensor, tokens: torch.Tensor, reverse: bool = Fals
     the last element of the result in scan order.  The reference has only
     the zero state.
     """
-    _lib.load()  # fail loudly before allocating if the library is missing
+    if not _fns:
+        _lib.load()  # fail loudly before allocating if the library is missing
     if out is None:
         out = torch.empty_like(tokens)
     if initial_state is None:
@@ -153,10 +214,9 @@ def scan_forward(gates: torch.Tensor, tokens: torch.Tensor, reverse: bool = Fals
     validate(gates, tokens, out)
     h0 = _check_state(initial_state, tokens)
     b, d, l = tokens.shape
-    with torch.cuda.device(tokens.device):
-        _lib.call("fpscan_scan_fwd_init", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
-                  h0.data_ptr(), b, d, l, DTYPE_CODES[tokens.dtype], 1 if reverse else 0,
-                  _stream_ptr(tokens.device))
+    _launch(tokens.get_device(), "fpscan_scan_fwd_init", gates.data_ptr(), tokens.data_ptr(),
+            out.data_ptr(), h0.data_ptr(), b, d, l, DTYPE_CODES[tokens.dtype],
+            1 if reverse else 0)
     return out
 
 
@@ -164,15 +224,15 @@ def scan_backward(gates: torch.Tensor, y: torch.Tensor, grad_output: torch.Tenso
     """Fused gradient of ``y = scan_forward(gates, tokens)``: one launch
     returning ``(grad_gates, grad_tokens)``.  Equals the reference's
     PScan.backward composition (fpscan/ops.py:70-83)."""
-    validate(gates, grad_output)
-    validate(gates, y)
+    if not (_fast_valid(gates, grad_output) and _fast_valid(gates, y)):
+        validate(gates, grad_output)
+        validate(gates, y)
     dgates = torch.empty_like(grad_output)
     dtokens = torch.empty_like(grad_output)
     b, d, l = grad_output.shape
-    with torch.cuda.device(grad_output.device):
-        _lib.call("fpscan_scan_bwd", gates.data_ptr(), y.data_ptr(), grad_output.data_ptr(),
-                  dgates.data_ptr(), dtokens.data_ptr(), b, d, l,
-                  DTYPE_CODES[grad_output.dtype], _stream_ptr(grad_output.device))
+    _launch(grad_output.get_device(), "fpscan_scan_bwd", gates.data_ptr(), y.data_ptr(),
+            grad_output.data_ptr(), dgates.data_ptr(), dtokens.data_ptr(), b, d, l,
+            DTYPE_CODES[grad_output.dtype])
     return dgates, dtokens
 
 
@@ -215,11 +275,9 @@ class PScanWithState(torch.autograd.Function):
         dgates = torch.empty_like(grad_output)
         dtokens = torch.empty_like(grad_output)
         zero = torch.zeros_like(h0f)
-        with torch.cuda.device(grad_output.device):
-            _lib.call("fpscan_shard_bwd_scan", gates.data_ptr(), out.data_ptr(),
-                      grad_output.data_ptr(), dgates.data_ptr(), dtokens.data_ptr(),
-                      zero.data_ptr(), h0f.data_ptr(), b * d, l,
-                      DTYPE_CODES[grad_output.dtype], _stream_ptr(grad_output.device))
+        _launch(grad_output.get_device(), "fpscan_shard_bwd_scan", gates.data_ptr(),
+                out.data_ptr(), grad_output.data_ptr(), dgates.data_ptr(), dtokens.data_ptr(),
+                zero.data_ptr(), h0f.data_ptr(), b * d, l, DTYPE_CODES[grad_output.dtype])
         dh0 = (gates[..., 0].float() * dtokens[..., 0].float()).to(ctx.h0_dtype)
         return dgates, dtokens, dh0
 
@@ -255,10 +313,8 @@ def scan_forward_gated(z: torch.Tensor, tokens: torch.Tensor, activation: str = 
     if out is None:
         out = torch.empty_like(tokens)
     b, d, l = tokens.shape
-    with torch.cuda.device(tokens.device):
-        _lib.call("fpscan_scan_fwd_act", z.data_ptr(), tokens.data_ptr(), out.data_ptr(), b, d, l,
-                  DTYPE_CODES[tokens.dtype], 1 if reverse else 0, code,
-                  _stream_ptr(tokens.device))
+    _launch(tokens.get_device(), "fpscan_scan_fwd_act", z.data_ptr(), tokens.data_ptr(),
+            out.data_ptr(), b, d, l, DTYPE_CODES[tokens.dtype], 1 if reverse else 0, code)
     return out
 
 
@@ -281,10 +337,9 @@ class PScanGated(torch.autograd.Function):
         dz = torch.empty_like(grad_output)
         dtokens = torch.empty_like(grad_output)
         b, d, l = grad_output.shape
-        with torch.cuda.device(grad_output.device):
-            _lib.call("fpscan_scan_bwd_act", z.data_ptr(), out.data_ptr(), grad_output.data_ptr(),
-                      dz.data_ptr(), dtokens.data_ptr(), b, d, l, DTYPE_CODES[grad_output.dtype],
-                      ctx.code, _stream_ptr(grad_output.device))
+        _launch(grad_output.get_device(), "fpscan_scan_bwd_act", z.data_ptr(), out.data_ptr(),
+                grad_output.data_ptr(), dz.data_ptr(), dtokens.data_ptr(), b, d, l,
+                DTYPE_CODES[grad_output.dtype], ctx.code)
         return dz, dtokens, None
 
 
@@ -305,10 +360,8 @@ def scan_forward_anylen(gates: torch.Tensor, tokens: torch.Tensor, reverse: bool
     if out is None:
         out = torch.empty_like(tokens)
     b, d, l = tokens.shape
-    with torch.cuda.device(tokens.device):
-        _lib.call("fpscan_scan_fwd_anylen", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(),
-                  b, d, l, DTYPE_CODES[tokens.dtype], 1 if reverse else 0,
-                  _stream_ptr(tokens.device))
+    _launch(tokens.get_device(), "fpscan_scan_fwd_anylen", gates.data_ptr(), tokens.data_ptr(),
+            out.data_ptr(), b, d, l, DTYPE_CODES[tokens.dtype], 1 if reverse else 0)
     return out
 
 
@@ -319,10 +372,9 @@ def scan_backward_anylen(gates: torch.Tensor, out: torch.Tensor, grad_output: to
     dgates = torch.empty_like(grad_output)
     dtokens = torch.empty_like(grad_output)
     b, d, l = grad_output.shape
-    with torch.cuda.device(grad_output.device):
-        _lib.call("fpscan_scan_bwd_anylen", gates.data_ptr(), out.data_ptr(),
-                  grad_output.data_ptr(), dgates.data_ptr(), dtokens.data_ptr(), b, d, l,
-                  DTYPE_CODES[grad_output.dtype], _stream_ptr(grad_output.device))
+    _launch(grad_output.get_device(), "fpscan_scan_bwd_anylen", gates.data_ptr(), out.data_ptr(),
+            grad_output.data_ptr(), dgates.data_ptr(), dtokens.data_ptr(), b, d, l,
+            DTYPE_CODES[grad_output.dtype])
     return dgates, dtokens
 
 
@@ -368,12 +420,10 @@ def validate_channels_last(gates: torch.Tensor, tokens: torch.Tensor,
             raise RuntimeError("out must be contiguous")
 
 
-def _cl_workspace(t: torch.Tensor, backward: bool):
+def _cl_workspace(t: torch.Tensor, backward: bool) -> torch.Tensor:
     b, l, d = t.shape
-    lib = _lib.load()
-    nbytes = lib.fpscan_cl_workspace_bytes(b, l, d, DTYPE_CODES[t.dtype], 1 if backward else 0)
-    stream = _stream_ptr(t.device)
-    return _workspace(t.device, stream, nbytes, kind="channels_last"), stream
+    nbytes = _fn("fpscan_cl_workspace_bytes")(b, l, d, DTYPE_CODES[t.dtype], 1 if backward else 0)
+    return _workspace(t.device, _raw_stream(t.get_device()), nbytes, kind="channels_last")
 
 
 def scan_forward_channels_last(gates: torch.Tensor, tokens: torch.Tensor, reverse: bool = False,
@@ -392,11 +442,10 @@ def scan_forward_channels_last(gates: torch.Tensor, tokens: torch.Tensor, revers
     b, l, d = tokens.shape
     if b == 0 or d == 0:
         return out
-    with torch.cuda.device(tokens.device):
-        ws, stream = _cl_workspace(tokens, False)
-        _lib.call("fpscan_scan_fwd_cl", gates.data_ptr(), tokens.data_ptr(), out.data_ptr(), b, l,
-                  d, DTYPE_CODES[tokens.dtype], 1 if reverse else 0, ws.data_ptr(), ws.numel(),
-                  stream)
+    ws = _cl_workspace(tokens, False)
+    _launch(tokens.get_device(), "fpscan_scan_fwd_cl", gates.data_ptr(), tokens.data_ptr(),
+            out.data_ptr(), b, l, d, DTYPE_CODES[tokens.dtype], 1 if reverse else 0,
+            ws.data_ptr(), ws.numel())
     return out
 
 
@@ -410,11 +459,10 @@ def scan_backward_channels_last(gates: torch.Tensor, out: torch.Tensor,
     b, l, d = grad_output.shape
     if b == 0 or d == 0:
         return dgates, dtokens
-    with torch.cuda.device(grad_output.device):
-        ws, stream = _cl_workspace(grad_output, True)
-        _lib.call("fpscan_scan_bwd_cl", gates.data_ptr(), out.data_ptr(), grad_output.data_ptr(),
-                  dgates.data_ptr(), dtokens.data_ptr(), b, l, d,
-                  DTYPE_CODES[grad_output.dtype], ws.data_ptr(), ws.numel(), stream)
+    ws = _cl_workspace(grad_output, True)
+    _launch(grad_output.get_device(), "fpscan_scan_bwd_cl", gates.data_ptr(), out.data_ptr(),
+            grad_output.data_ptr(), dgates.data_ptr(), dtokens.data_ptr(), b, l, d,
+            DTYPE_CODES[grad_output.dtype], ws.data_ptr(), ws.numel())
     return dgates, dtokens
 
 
