@@ -23,6 +23,8 @@
 // sequence-sharded multi-GPU mode.  Without `init` the gate of a row's first
 // element is ignored, exactly like the reference's forced 1.0
 // (csrc/full_scan/full_scan.cu:96).
+#include <cstdlib>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -53,8 +55,12 @@ struct FwdKParams {
   int lg;  // log2(seqlen)
 };
 
+// DIRECT: no shared-memory staging -- every thread loads its vectors from
+// global memory itself.  Used for small launches whose rows fit in one
+// chunk, where the staging pipeline's set-up (mbarrier init, one thread
+// issuing the copies, waiting) is a visible share of a few-microsecond kernel.
 template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT,
-          int ACT>
+          int ACT, bool DIRECT = false>
 __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fwd_kernel(const FwdKParams p) {
   constexpr int V = Elem<T>::kVec;   // elements per 16-byte vector
   constexpr int E = V * NV;          // elements per thread per chunk
@@ -89,12 +95,14 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
   const int wwidth = tpr < 32 ? tpr : 32;
   const int seg_warps = tpr >> 5;
 
-  if (tid == 0) {
+  if (!DIRECT) {
+    if (tid == 0) {
 #pragma unroll
-    for (int s = 0; s < S; ++s) mbar_init(&s_bar[s], 1);
-    fence_mbar_init();
+      for (int s = 0; s < S; ++s) mbar_init(&s_bar[s], 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
   }
-  __syncthreads();
 
   // Thread 0 issues chunk loads; `issued` counts them.
   int64_t issued = 0;
@@ -108,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     bulk_g2s(s_g[s], gates + base + off, bytes, &s_bar[s]);
     bulk_g2s(s_x[s], tokens + base + off, bytes, &s_bar[s]);
   };
-  if (tid == 0) {
+  if (!DIRECT && tid == 0) {
     for (; issued < min((int64_t)S, nck); ++issued) issue(issued);
   }
 
@@ -127,15 +135,25 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     const int64_t cnt = min((int64_t)CH, n - off);
     const bool valid = ((int64_t)vi << LGE) < cnt;
 
-    const bool ok = mbar_wait_bounded(&s_bar[s], phase);
+    const bool ok = DIRECT || mbar_wait_bounded(&s_bar[s], phase);
 
     float a[E], b[E];
     if (valid) {
       Vec16<T> gv[NV], xv[NV];
       {
         uint4 rg[NV], rx[NV];
-        lds_vecs<NV>(&s_g[s][vi * NV], rg);
-        lds_vecs<NV>(&s_x[s][vi * NV], rx);
+        if (DIRECT) {
+          const uint4* gsrc = reinterpret_cast<const uint4*>(gates + base + off) + vi * NV;
+          const uint4* xsrc = reinterpret_cast<const uint4*>(tokens + base + off) + vi * NV;
+#pragma unroll
+          for (int q = 0; q < NV; ++q) {
+            rg[q] = __ldg(gsrc + q);
+            rx[q] = __ldg(xsrc + q);
+          }
+        } else {
+          lds_vecs<NV>(&s_g[s][vi * NV], rg);
+          lds_vecs<NV>(&s_x[s][vi * NV], rx);
+        }
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
           gv[q].raw = rg[q];
@@ -173,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
       break;
     }
     // Every thread has consumed stage s: refill it.
-    if (tid == 0 && issued < nck) {
+    if (!DIRECT && tid == 0 && issued < nck) {
       issue(issued);
       ++issued;
     }
@@ -242,10 +260,10 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
 // One wave of CTAs: tiles = SMs x resident CTAs per SM (queried once per
 // device and kernel), each a contiguous run of whole rows.
 template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT,
-          int ACT>
+          int ACT, bool DIRECT = false>
 static cudaError_t launch_fwd_t(const FwdArgs& a) {
-  constexpr int smem = FwdCfg<T, NV>::smem_bytes();
-  auto kern = scan_fwd_kernel<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT>;
+  constexpr int smem = DIRECT ? 0 : FwdCfg<T, NV>::smem_bytes();
+  auto kern = scan_fwd_kernel<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT, DIRECT>;
   static int occ_cache[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -262,6 +280,13 @@ static cudaError_t launch_fwd_t(const FwdArgs& a) {
   const int64_t slots = (int64_t)a.num_sms * occ;
   int64_t rpt = (a.rows + slots - 1) / slots;
   if (rpt < 1) rpt = 1;
+  // Plain scans whose every tile is a single chunk (one wave of small
+  // tiles) run the direct-load variant.
+  if constexpr (!DIRECT && HAS_OUT && !HAS_INIT && !HAS_CARRY_OUT && ACT == kActNone) {
+    constexpr int64_t kChunk = (int64_t)kThreads * Elem<T>::kVec * NV;
+    if (rpt * a.seqlen <= kChunk && !getenv("FPSCAN_B200_NO_DIRECT"))
+      return launch_fwd_t<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT, true>(a);
+  }
   const int64_t tiles = (a.rows + rpt - 1) / rpt;
   FwdKParams p{a.gates, a.tokens, a.out, a.init, a.carry_a, a.carry_b, a.rows, rpt,
                ilog2_host(a.seqlen)};
