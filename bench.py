@@ -503,7 +503,7 @@ def run_shard_seq(args, cfg):
 
     def step():
         if world > 1:
-            y = seq_sharded_pscan(g, x)
+            y = seq_sharded_pscan(g, x, mode=args.seq_mode)
         else:
             y = fpscan_b200.pscan(g, x)
         torch.autograd.grad(y, (g, x), go)
@@ -528,9 +528,10 @@ def run_shard_seq(args, cfg):
             "config": {"workload": f"shard_seq: pscan fwd+bwd fp32 batch={B} dim={D} seqlen={L}, "
                                    f"seqlen split over {world} GPU(s)",
                        "batch": B, "dim": D, "seqlen": L, "parallelism": f"seq-shard x{world}",
+                       "seq_mode": args.seq_mode if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (no flush)"},
             "pct_of_hbm_peak": round(100 * value / world / peak, 2), "peak_source": peak_kind,
-            "gpu_launches": (6 if world > 1 else 2) * args.steps,
+            "gpu_launches": (2 if world == 1 or args.seq_mode != "allgather" else 6) * args.steps,
             "clocks": clock_info, "device_status": _lib.device_status()}), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -683,6 +684,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seq-mode", choices=["auto", "chain", "allgather"], default="auto",
+                    help="shard_seq: carry exchange (chain: rank to rank over NVLink inside the "
+                         "kernels; allgather: reduce + NCCL all-gather + scan)")
     ap.add_argument("--max-shapes", type=int, default=None,
                     help="anylen / channels_last: only the first N shapes of the table")
     args = ap.parse_args()

@@ -40,6 +40,16 @@ SIGNATURES = {
     "fpscan_shard_bwd_reduce": [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_bwd_scan": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_carry_combine": [_vp, _c_int, _c_int, _c_i64, _c_int, _vp, _vp],
+    "fpscan_link_bytes": [_c_i64, _c_int],
+    "fpscan_link_create": [_c_i64, _c_int, ctypes.POINTER(_vp)],
+    "fpscan_link_destroy": [_vp],
+    "fpscan_link_ipc_handle": [_vp, ctypes.c_char_p],
+    "fpscan_link_open": [ctypes.c_char_p, ctypes.POINTER(_vp)],
+    "fpscan_link_close": [_vp],
+    "fpscan_shard_fwd_link": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp, _vp, _vp,
+                              ctypes.c_uint32, _c_int, _vp],
+    "fpscan_shard_bwd_link": [_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp, _vp,
+                              _vp, ctypes.c_uint32, _c_int, _vp],
     "fpscan_last_error": [],
     "fpscan_device_status": [ctypes.POINTER(ctypes.c_uint), _c_int],
 }
@@ -72,7 +82,8 @@ def load() -> ctypes.CDLL:
             fn.argtypes = argtypes
             fn.restype = {"fpscan_last_error": ctypes.c_char_p,
                           "fpscan_scan_fwd_workspace_bytes": ctypes.c_int64,
-                          "fpscan_cl_workspace_bytes": ctypes.c_int64}.get(name, ctypes.c_int)
+                          "fpscan_cl_workspace_bytes": ctypes.c_int64,
+                          "fpscan_link_bytes": ctypes.c_int64}.get(name, ctypes.c_int)
         ver = lib.fpscan_abi_version()
         if ver != EXPECTED_ABI_VERSION:
             raise ImportError(f"libfpscan_b200 ABI version {ver}, expected {EXPECTED_ABI_VERSION}")

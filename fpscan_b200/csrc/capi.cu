@@ -11,6 +11,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <cstdlib>
 #include <string>
 
@@ -621,6 +622,189 @@ int fpscan_scan_bwd_cl(const void* gates, const void* y, const void* grad_out, v
   a.backward = 1;
   a.stream = static_cast<cudaStream_t>(stream);
   return cuda_result(launch_cl(a), "fpscan_scan_bwd_cl launch");
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ rank links
+// Mailbox of one rank (cudaMalloc'd once per (rows, depth); 256-byte aligned
+// regions, 4-byte words):
+//   fwd_val[depth][rows] fwd_flag[depth][rows]   forward values from rank r-1
+//   bwd_val[depth][rows] bwd_flag[depth][rows]   backward values from rank r+1
+//   fwd_ack[rows]   epochs of forward values rank r+1 has consumed
+//   bwd_ack[rows]   epochs of backward values rank r-1 has consumed
+//   zeros[rows]     never written
+// A call with epoch e uses ring slot e % depth; epochs start at 1 and are
+// counted per direction, so a producer waits for ack >= e - depth.
+namespace {
+struct MailboxLayout {
+  int64_t fwd_val, fwd_flag, bwd_val, bwd_flag, fwd_ack, bwd_ack, zeros, total;
+};
+MailboxLayout mailbox_layout(int64_t rows, int depth) {
+  auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
+  const int64_t ring = up((int64_t)depth * rows * 4), one = up(rows * 4);
+  MailboxLayout m;
+  m.fwd_val = 0;
+  m.fwd_flag = m.fwd_val + ring;
+  m.bwd_val = m.fwd_flag + ring;
+  m.bwd_flag = m.bwd_val + ring;
+  m.fwd_ack = m.bwd_flag + ring;
+  m.bwd_ack = m.fwd_ack + one;
+  m.zeros = m.bwd_ack + one;
+  m.total = m.zeros + one;
+  return m;
+}
+template <typename P>
+P* at(void* base, int64_t off) {
+  return reinterpret_cast<P*>(static_cast<char*>(base) + off);
+}
+int check_link(int64_t rows, int depth) {
+  if (rows <= 0 || rows > (int64_t(1) << 31))
+    return fail(FPSCAN_ERR_INVALID, "link rows must be in [1, 2^31] (got %lld)", (long long)rows);
+  if (depth < 1 || depth > 64)
+    return fail(FPSCAN_ERR_INVALID, "link depth must be in [1, 64] (got %d)", depth);
+  return FPSCAN_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int64_t fpscan_link_bytes(int64_t rows, int depth) {
+  if (check_link(rows, depth) != FPSCAN_OK) return 0;
+  return mailbox_layout(rows, depth).total;
+}
+
+int fpscan_link_create(int64_t rows, int depth, void** mailbox) {
+  FPSCAN_TRY(check_link(rows, depth));
+  if (mailbox == nullptr) return fail(FPSCAN_ERR_INVALID, "mailbox is NULL");
+  const int64_t bytes = mailbox_layout(rows, depth).total;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, (size_t)bytes);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return cuda_result(e, "fpscan_link_create");
+  }
+  *mailbox = p;
+  return ok();
+}
+
+int fpscan_link_destroy(void* mailbox) {
+  if (mailbox == nullptr) return ok();
+  return cuda_result(cudaFree(mailbox), "fpscan_link_destroy");
+}
+
+int fpscan_link_ipc_handle(void* mailbox, void* handle) {
+  if (mailbox == nullptr || handle == nullptr)
+    return fail(FPSCAN_ERR_INVALID, "mailbox and handle must not be NULL");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, mailbox);
+  if (e != cudaSuccess) return cuda_result(e, "fpscan_link_ipc_handle");
+  memcpy(handle, &h, sizeof(h));
+  return ok();
+}
+
+int fpscan_link_open(const void* handle, void** peer_mailbox) {
+  if (handle == nullptr || peer_mailbox == nullptr)
+    return fail(FPSCAN_ERR_INVALID, "handle and peer_mailbox must not be NULL");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_result(e, "fpscan_link_open");
+  *peer_mailbox = p;
+  return ok();
+}
+
+int fpscan_link_close(void* peer_mailbox) {
+  if (peer_mailbox == nullptr) return ok();
+  return cuda_result(cudaIpcCloseMemHandle(peer_mailbox), "fpscan_link_close");
+}
+
+int fpscan_shard_fwd_link(const void* gates, const void* tokens, void* out, float* init_record,
+                          int64_t rows, int64_t seqlen, int dtype, void* local, void* prev,
+                          void* next, uint32_t epoch, int depth, void* stream) {
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_link(rows, depth));
+  if (local == nullptr) return fail(FPSCAN_ERR_INVALID, "local mailbox is NULL");
+  if (prev == nullptr && next == nullptr)
+    return fail(FPSCAN_ERR_INVALID, "a linked scan needs an upstream or a downstream rank");
+  if (epoch == 0) return fail(FPSCAN_ERR_INVALID, "epoch 0 is reserved");
+  const int nv = tuned_nv(true, dtype) == 1 ? 1 : 2;
+  const int64_t chunk = (int64_t)kThreads * (16 / dtype_size(dtype)) * nv;
+  if (!is_pow2(seqlen) || seqlen <= chunk || seqlen > kShardMaxL)
+    return fail(FPSCAN_ERR_INVALID,
+                "linked scan: local seqlen must be a power of 2 > %lld and <= %lld (got %lld)",
+                (long long)chunk, (long long)kShardMaxL, (long long)seqlen);
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(tokens, "tokens"));
+  FPSCAN_TRY(check_ptr(out, "out"));
+  const MailboxLayout m = mailbox_layout(rows, depth);
+  const int64_t slot = (int64_t)(epoch % (uint32_t)depth) * rows;
+  FwdArgs a{gates, tokens, out, nullptr, nullptr, nullptr, rows, seqlen, dtype, 0,
+            num_sms_current(), static_cast<cudaStream_t>(stream)};
+  a.nv = nv;
+  a.link = (prev ? 1 : 0) | (next ? 2 : 0);
+  a.lk.epoch = epoch;
+  a.lk.depth = (uint32_t)depth;
+  if (prev) {
+    a.lk.in_val = at<float>(local, m.fwd_val) + slot;
+    a.lk.in_flag = at<uint32_t>(local, m.fwd_flag) + slot;
+    a.lk.ack_out = at<uint32_t>(prev, m.fwd_ack);
+    a.lk.in_record = init_record;
+  }
+  if (next) {
+    a.lk.out_val = at<float>(next, m.fwd_val) + slot;
+    a.lk.out_flag = at<uint32_t>(next, m.fwd_flag) + slot;
+    a.lk.ack_in = at<uint32_t>(local, m.fwd_ack);
+  }
+  return cuda_result(launch_fwd(a), "fpscan_shard_fwd_link launch");
+}
+
+int fpscan_shard_bwd_link(const void* gates, const void* y, const void* grad_out, void* dgates,
+                          void* dtokens, const float* y_prev, int64_t rows, int64_t seqlen,
+                          int dtype, void* local, void* prev, void* next, uint32_t epoch,
+                          int depth, void* stream) {
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_link(rows, depth));
+  if (local == nullptr) return fail(FPSCAN_ERR_INVALID, "local mailbox is NULL");
+  if (prev == nullptr && next == nullptr)
+    return fail(FPSCAN_ERR_INVALID, "a linked scan needs an upstream or a downstream rank");
+  if (epoch == 0) return fail(FPSCAN_ERR_INVALID, "epoch 0 is reserved");
+  if (prev != nullptr && y_prev == nullptr)
+    return fail(FPSCAN_ERR_INVALID, "y_prev is required on every rank but the first");
+  const int nv = 2;
+  const int64_t chunk = (int64_t)kThreads * (16 / dtype_size(dtype)) * nv;
+  if (!is_pow2(seqlen) || seqlen <= chunk || seqlen > kShardMaxL)
+    return fail(FPSCAN_ERR_INVALID,
+                "linked backward: local seqlen must be a power of 2 > %lld and <= %lld (got %lld)",
+                (long long)chunk, (long long)kShardMaxL, (long long)seqlen);
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(y, "y"));
+  FPSCAN_TRY(check_ptr(grad_out, "grad_out"));
+  FPSCAN_TRY(check_ptr(dgates, "dgates"));
+  FPSCAN_TRY(check_ptr(dtokens, "dtokens"));
+  const MailboxLayout m = mailbox_layout(rows, depth);
+  const int64_t slot = (int64_t)(epoch % (uint32_t)depth) * rows;
+  BwdArgs a{gates,   y,       grad_out, dgates, dtokens, nullptr, nullptr,
+            nullptr, rows,    seqlen,   dtype,  num_sms_current(),
+            static_cast<cudaStream_t>(stream)};
+  a.nv = nv;
+  a.y_prev = y_prev ? y_prev : at<float>(local, m.zeros);
+  a.link = (next ? 1 : 0) | (prev ? 2 : 0);
+  a.lk.epoch = epoch;
+  a.lk.depth = (uint32_t)depth;
+  if (next) {
+    a.lk.in_val = at<float>(local, m.bwd_val) + slot;
+    a.lk.in_flag = at<uint32_t>(local, m.bwd_flag) + slot;
+    a.lk.ack_out = at<uint32_t>(next, m.bwd_ack);
+  }
+  if (prev) {
+    a.lk.out_val = at<float>(prev, m.bwd_val) + slot;
+    a.lk.out_flag = at<uint32_t>(prev, m.bwd_flag) + slot;
+    a.lk.ack_in = at<uint32_t>(local, m.bwd_ack);
+  }
+  return cuda_result(launch_bwd(a), "fpscan_shard_bwd_link launch");
 }
 
 }  // extern "C"

@@ -25,7 +25,12 @@ constexpr int kWarps = kThreads / 32;
 // Device-side status word.  Bounded waits that give up set a bit here instead
 // of hanging the GPU; the host reads and clears it through
 // fpscan_device_status().
-enum : unsigned { kStatusWaitTimeout = 1u, kStatusLookbackTimeout = 2u, kStatusMisaligned = 4u };
+enum : unsigned {
+  kStatusWaitTimeout = 1u,
+  kStatusLookbackTimeout = 2u,
+  kStatusMisaligned = 4u,
+  kStatusLinkTimeout = 8u,
+};
 
 extern __device__ unsigned int g_status;
 
@@ -114,6 +119,42 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
       atomicOr(&g_status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- rank links
+// Cross-GPU hand-off of per-row values over NVLink peer memory (chained
+// sequence sharding).  The producer stores the value and then releases the
+// row's flag (the epoch of the call) at system scope; the consumer acquires
+// the flag and reads the value bypassing L1.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ float ld_relaxed_sys(const float* p) {
+  float v;
+  asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(float* p, float v) {
+  asm volatile("st.relaxed.sys.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+// Wait (bounded, 2 s) until the epoch-tagged word at p reaches `epoch`
+// (wrap-safe comparison).  On timeout records kStatusLinkTimeout, returns false.
+__device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t epoch) {
+  if ((int)(ld_acquire_sys(p) - epoch) >= 0) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 0;; ++it) {
+    if ((int)(ld_acquire_sys(p) - epoch) >= 0) return true;
+    if ((it & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
+      atomicOr(&g_status, kStatusLinkTimeout);
       return false;
     }
   }

@@ -17,6 +17,26 @@ inline int ilog2_host(int64_t v) {
   return r;
 }
 
+// Chained sequence sharding: per-row hand-off between neighbouring ranks
+// through peer-mapped memory (see fpscan_link_* in capi.cu for the layout).
+// in_*: values arriving from the upstream rank (local memory); ack_out: the
+// upstream rank's ack word per row (peer memory), set to the epoch once the
+// value is consumed.  out_*: the downstream rank's slot (peer memory);
+// ack_in: this rank's ack words written by the downstream rank.  The out
+// value of a row is written only after ack_in shows the slot's previous use
+// (epoch - depth) consumed.
+struct LinkParams {
+  const float* in_val = nullptr;
+  const uint32_t* in_flag = nullptr;
+  uint32_t* ack_out = nullptr;
+  float* out_val = nullptr;
+  uint32_t* out_flag = nullptr;
+  const uint32_t* ack_in = nullptr;
+  float* in_record = nullptr;  // optional: received values are also stored here
+  uint32_t epoch = 0;
+  uint32_t depth = 1;
+};
+
 struct FwdArgs {
   const void* gates;
   const void* tokens;
@@ -32,6 +52,8 @@ struct FwdArgs {
   cudaStream_t stream;
   int nv = 2;           // 16-byte vectors per thread per chunk (1 or 2)
   int act = 0;          // gate activation applied on load (Act); plain scan only
+  int link = 0;         // bit 0: init from link.in_*; bit 1: final state to link.out_*
+  LinkParams lk;
 };
 
 struct BwdArgs {
@@ -50,6 +72,8 @@ struct BwdArgs {
   cudaStream_t stream;
   int nv = 2;           // 16-byte vectors per thread per chunk (1 or 2)
   int act = 0;          // gate activation (Act): dgates becomes d/dz; plain backward only
+  int link = 0;         // bit 0: addend from link.in_*; bit 1: carry to link.out_*
+  LinkParams lk;
 };
 
 struct SplitArgs {

@@ -48,9 +48,15 @@ struct BwdKParams {
   int64_t rows;
   int64_t rows_per_tile;
   int lg;
+  LinkParams lk;
 };
 
-template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY, int ACT>
+// LINK (chained sequence sharding; multi-chunk rows): bit 0 -- the value
+// entering a row's last element (the downstream rank's gates[0]*dtokens[0])
+// arrives over the link (thread 0 waits, reads, acks, shares through shared
+// memory); bit 1 -- this rank's gates[0]*dtokens[0] of each row goes to the
+// upstream rank.  Link kernels always take y[-1] of each row from y_prev.
+template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY, int ACT, int LINK = 0>
 // Gated variants with two vectors per thread hold more live values: they get
 // a 2-CTA register budget (128) instead of spilling under the 3-CTA one.
 __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : BwdCfg<NV>::kMinBlocks)
@@ -70,6 +76,7 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
   uint4* s_y = s_go + S * SV;     // [S][YS]   (HAS_OUT only)
   __shared__ __align__(8) uint64_t s_bar[S];
   __shared__ float2 s_wt[2][kWarps];
+  __shared__ float s_link[2];  // LINK bit 0: value entering the row, by chunk parity
 
   const T* __restrict__ gates = static_cast<const T*>(p.gates);
   const T* __restrict__ y = static_cast<const T*>(p.y);
@@ -197,6 +204,14 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
     warp_exclusive(ta, tb, lane, wwidth, pa, pb);
     const int buf = (int)(k & 1);
     if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
+    if constexpr ((LINK & 1) != 0) {
+      if (tid == 0 && multi && (((off + CH) & Lmask) == 0)) {
+        const int64_t lrow = row0 + (off >> lg);
+        wait_epoch(p.lk.in_flag + lrow, p.lk.epoch);
+        s_link[buf] = ld_relaxed_sys(p.lk.in_val + lrow);
+        st_release_sys(p.lk.ack_out + lrow, p.lk.epoch);  // the slot may be reused
+      }
+    }
 
     if (__syncthreads_or(!ok)) {
       aborted = true;
@@ -216,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
     bool skip_state = false;
     if (row_start) {
       if (HAS_CARRY) {
-        carry = p.addend[row];
+        carry = (LINK & 1) ? s_link[buf] : p.addend[row];
         state = fmaf(pa, carry, pb);
       } else {
         carry = 0.f;
@@ -234,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
     if (valid) {
       if (HAS_OUT) {
         float yp_first = y_before;
-        if (grp_row_first) yp_first = HAS_CARRY ? p.y_prev[row] : 0.f;
+        if (grp_row_first) yp_first = (HAS_CARRY || LINK != 0) ? p.y_prev[row] : 0.f;
         float f_dt[E], f_dg[E];  // memory order
 #pragma unroll
         for (int i = 0; i < E; ++i) {
@@ -257,6 +272,14 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
           d1[q] = pack_vec<T>(f_dt + q * V);
           d2[q] = pack_vec<T>(f_dg + q * V);
         }
+        if constexpr ((LINK & 2) != 0) {
+          if (grp_row_first) {
+            const float v = Elem<T>::load(gv[0].e[0]) * dt[E - 1];
+            wait_epoch(p.lk.ack_in + row, p.lk.epoch - p.lk.depth);  // slot's last use consumed
+            st_relaxed_sys(p.lk.out_val + row, v);
+            st_release_sys(p.lk.out_flag + row, p.lk.epoch);
+          }
+        }
       } else if (grp_row_first) {
         p.carry_b[row] = Elem<T>::load(gv[0].e[0]) * dt[E - 1];  // plain scan only
       }
@@ -276,10 +299,10 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
   }
 }
 
-template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY, int ACT>
+template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY, int ACT, int LINK = 0>
 static cudaError_t launch_bwd_t(const BwdArgs& a) {
   constexpr int smem = BwdCfg<NV>::template smem_bytes<HAS_OUT>();
-  auto kern = scan_bwd_kernel<T, NV, HAS_OUT, HAS_CARRY, ACT>;
+  auto kern = scan_bwd_kernel<T, NV, HAS_OUT, HAS_CARRY, ACT, LINK>;
   // Per device: opt in to >48 KiB of dynamic shared memory and cache the
   // number of resident CTAs.
   static int occ_cache[64] = {0};
@@ -300,7 +323,7 @@ static cudaError_t launch_bwd_t(const BwdArgs& a) {
   if (rpt < 1) rpt = 1;
   const int64_t tiles = (a.rows + rpt - 1) / rpt;
   BwdKParams p{a.gates, a.y, a.grad_out, a.dgates, a.dtokens, a.addend, a.y_prev, a.carry_b,
-               a.rows, rpt, ilog2_host(a.seqlen)};
+               a.rows, rpt, ilog2_host(a.seqlen), a.lk};
   kern<<<(unsigned)tiles, kThreads, smem, a.stream>>>(p);
   return cudaGetLastError();
 }
@@ -313,8 +336,31 @@ static cudaError_t launch_bwd_nv(const BwdArgs& a) {
                    : launch_bwd_t<T, 2, HAS_OUT, HAS_CARRY, ACT>(a);
 }
 
+// Chained sequence sharding: link bit 0 (value entering from downstream)
+// implies HAS_CARRY; one or two vectors per thread.
+template <typename T, int LINK>
+static cudaError_t launch_bwd_link_t(const BwdArgs& a) {
+  constexpr bool kCarry = (LINK & 1) != 0;
+  return a.nv == 1 ? launch_bwd_t<T, 1, true, kCarry, kActNone, LINK>(a)
+                   : launch_bwd_t<T, 2, true, kCarry, kActNone, LINK>(a);
+}
+
 template <typename T>
 static cudaError_t launch_bwd_dtype(const BwdArgs& a) {
+  if (a.link != 0) {
+    if (a.act != kActNone || a.dtokens == nullptr || a.y_prev == nullptr)
+      return cudaErrorInvalidValue;
+    switch (a.link) {
+      case 1:
+        return launch_bwd_link_t<T, 1>(a);
+      case 2:
+        return launch_bwd_link_t<T, 2>(a);
+      case 3:
+        return launch_bwd_link_t<T, 3>(a);
+      default:
+        return cudaErrorInvalidValue;
+    }
+  }
   const bool has_out = a.dtokens != nullptr;
   const bool has_carry = a.addend != nullptr;
   if (has_out && !has_carry) {

@@ -53,14 +53,22 @@ struct FwdKParams {
   int64_t rows;
   int64_t rows_per_tile;
   int lg;  // log2(seqlen)
+  LinkParams lk;
 };
 
 // DIRECT: no shared-memory staging -- every thread loads its vectors from
 // global memory itself.  Used for small launches whose rows fit in one
 // chunk, where the staging pipeline's set-up (mbarrier init, one thread
 // issuing the copies, waiting) is a visible share of a few-microsecond kernel.
+//
+// LINK (chained sequence sharding; multi-chunk rows, forward order only):
+// bit 0 -- a row's initial state arrives from the upstream rank: at the row's
+// first chunk thread 0 waits for the row's flag, reads the value, marks it
+// consumed in the upstream rank's ack word and hands it to the CTA through
+// shared memory; bit 1 -- the row's final state goes to the downstream rank
+// (after its ack shows the ring slot free), released at system scope.
 template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT,
-          int ACT, bool DIRECT = false>
+          int ACT, bool DIRECT = false, int LINK = 0>
 __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fwd_kernel(const FwdKParams p) {
   constexpr int V = Elem<T>::kVec;   // elements per 16-byte vector
   constexpr int E = V * NV;          // elements per thread per chunk
@@ -75,6 +83,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
   uint4 (*s_x)[SV] = reinterpret_cast<uint4 (*)[SV]>(dsm + S * SV);  // [S][SV]
   __shared__ __align__(8) uint64_t s_bar[S];
   __shared__ float2 s_wt[2][kWarps];
+  __shared__ float s_link[2];  // LINK bit 0: the row's initial state, by chunk parity
 
   const T* __restrict__ gates = static_cast<const T*>(p.gates);
   const T* __restrict__ tokens = static_cast<const T*>(p.tokens);
@@ -185,6 +194,16 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     warp_exclusive(ta, tb, lane, wwidth, pa, pb);
     const int buf = (int)(k & 1);
     if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
+    if constexpr ((LINK & 1) != 0) {
+      if (tid == 0 && multi && ((off & Lmask) == 0)) {
+        const int64_t lrow = row0 + (off >> lg);
+        wait_epoch(p.lk.in_flag + lrow, p.lk.epoch);
+        const float v = ld_relaxed_sys(p.lk.in_val + lrow);
+        st_release_sys(p.lk.ack_out + lrow, p.lk.epoch);  // the slot may be reused
+        s_link[buf] = v;
+        if (p.lk.in_record) p.lk.in_record[lrow] = v;
+      }
+    }
 
     if (__syncthreads_or(!ok)) {
       aborted = true;
@@ -206,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     bool skip_state = false;
     if (row_start) {
       if (HAS_INIT) {
-        carry = p.init[row];
+        carry = (LINK & 1) ? s_link[buf] : p.init[row];
         state = fmaf(pa, carry, pb);
       } else {
         carry = 0.f;
@@ -238,6 +257,13 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
         p.carry_a[row] = acc_a;
         p.carry_b[row] = carry;
       }
+      if constexpr ((LINK & 2) != 0) {
+        if (tid == 0 && ((off + CH) & Lmask) == 0) {
+          wait_epoch(p.lk.ack_in + row, p.lk.epoch - p.lk.depth);  // slot's last use consumed
+          st_relaxed_sys(p.lk.out_val + row, carry);
+          st_release_sys(p.lk.out_flag + row, p.lk.epoch);
+        }
+      }
     } else if (HAS_CARRY_OUT && valid && seg_lane_t == tpr - 1) {
       p.carry_a[row] = pa * a[E - 1];
       p.carry_b[row] = yv[E - 1];
@@ -260,10 +286,10 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
 // One wave of CTAs: tiles = SMs x resident CTAs per SM (queried once per
 // device and kernel), each a contiguous run of whole rows.
 template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT,
-          int ACT, bool DIRECT = false>
+          int ACT, bool DIRECT = false, int LINK = 0>
 static cudaError_t launch_fwd_t(const FwdArgs& a) {
   constexpr int smem = DIRECT ? 0 : FwdCfg<T, NV>::smem_bytes();
-  auto kern = scan_fwd_kernel<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT, DIRECT>;
+  auto kern = scan_fwd_kernel<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT, DIRECT, LINK>;
   static int occ_cache[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -282,14 +308,15 @@ static cudaError_t launch_fwd_t(const FwdArgs& a) {
   if (rpt < 1) rpt = 1;
   // Plain scans whose every tile is a single chunk (one wave of small
   // tiles) run the direct-load variant.
-  if constexpr (!DIRECT && HAS_OUT && !HAS_INIT && !HAS_CARRY_OUT && ACT == kActNone) {
+  if constexpr (!DIRECT && LINK == 0 && HAS_OUT && !HAS_INIT && !HAS_CARRY_OUT &&
+                ACT == kActNone) {
     constexpr int64_t kChunk = (int64_t)kThreads * Elem<T>::kVec * NV;
     if (rpt * a.seqlen <= kChunk && !getenv("FPSCAN_B200_NO_DIRECT"))
       return launch_fwd_t<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT, true>(a);
   }
   const int64_t tiles = (a.rows + rpt - 1) / rpt;
   FwdKParams p{a.gates, a.tokens, a.out, a.init, a.carry_a, a.carry_b, a.rows, rpt,
-               ilog2_host(a.seqlen)};
+               ilog2_host(a.seqlen), a.lk};
   kern<<<(unsigned)tiles, kThreads, smem, a.stream>>>(p);
   return cudaGetLastError();
 }
@@ -316,8 +343,31 @@ static cudaError_t launch_fwd_act(const FwdArgs& a) {
   }
 }
 
+// Chained sequence sharding: link bit 0 (init from upstream) implies
+// HAS_INIT; one or two vectors per thread.
+template <typename T, int LINK>
+static cudaError_t launch_fwd_link_t(const FwdArgs& a) {
+  constexpr bool kInit = (LINK & 1) != 0;
+  return a.nv == 1 ? launch_fwd_t<T, 1, false, true, kInit, false, kActNone, false, LINK>(a)
+                   : launch_fwd_t<T, 2, false, true, kInit, false, kActNone, false, LINK>(a);
+}
+
 template <typename T>
 static cudaError_t launch_fwd_dtype(const FwdArgs& a) {
+  if (a.link != 0) {
+    if (a.reverse || a.act != kActNone || a.carry_a != nullptr || a.out == nullptr)
+      return cudaErrorInvalidValue;
+    switch (a.link) {
+      case 1:
+        return launch_fwd_link_t<T, 1>(a);
+      case 2:
+        return launch_fwd_link_t<T, 2>(a);
+      case 3:
+        return launch_fwd_link_t<T, 3>(a);
+      default:
+        return cudaErrorInvalidValue;
+    }
+  }
   const bool has_out = a.out != nullptr;
   const bool has_init = a.init != nullptr;
   const bool has_co = a.carry_a != nullptr;

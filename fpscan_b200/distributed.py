@@ -25,6 +25,18 @@ backward (dtokens[t] = gates[t+1]*dtokens[t+1] + g[t], dgates[t] = dtokens[t]*y[
   4. fused backward with that addend and y_init (= y of the previous shard's
      last element) for dgates at the first position.
 
+Chained mode (``seq_sharded_pscan(..., mode="chain")``, the default where it
+applies): the reduce passes and the all-gathers disappear.  Each rank's scan
+kernel waits, row by row, for the state entering the row from rank r-1 and
+hands the row's final state to rank r+1 as soon as the row is done, through
+per-rank mailboxes mapped into the neighbours with CUDA IPC (stores and
+loads over NVLink; system-scope release / acquire flags, bounded waits).
+The ranks run as a pipeline one row apart, each reading its shard once:
+forward 3*N*s and backward 5*N*s bytes per rank, as on one GPU.  The
+backward chain runs the other way; the state each rank received in the
+forward is y[-1] of its shard for dgates.  Needs one process per distinct
+GPU of one node and a local seqlen larger than one chunk.
+
 The device-side steps are behind ``LocalOps`` so the exchange logic can be
 exercised on CPU ranks (gloo) with a CPU implementation injected by tests;
 the default, ``CudaOps``, calls libfpscan_b200.so and is the only
@@ -32,6 +44,7 @@ implementation in this package.
 """
 from __future__ import annotations
 
+import socket
 from typing import Optional
 
 import torch
@@ -40,7 +53,10 @@ import torch.distributed as dist
 from . import _lib
 from .ops import DTYPE_CODES, pscan, scan_backward, scan_forward, validate
 
+import ctypes
+
 __all__ = [
+    "RankChain",
     "channel_slice",
     "channel_sharded_pscan",
     "seq_sharded_pscan",
@@ -182,15 +198,167 @@ class SeqShardedPScan(torch.autograd.Function):
         return dg, dt, None, None
 
 
+# --------------------------------------------------------------------------- chained mode
+class RankChain:
+    """Mailboxes linking this rank to ranks r-1 and r+1 (same rows on every
+    rank).  Collective to construct: every rank of ``group`` must create its
+    chain for the same ``rows`` in the same order.  ``depth`` ring slots per
+    direction bound how many chained calls one rank may run ahead of its
+    neighbour (the producer waits for the slot's previous use to be consumed)."""
+
+    def __init__(self, rows: int, device: torch.device, group=None, depth: int = 4):
+        self.lib = _lib.load()
+        self.group, self.rows, self.depth = group, rows, depth
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        idx = torch.device(device).index
+        # Linked kernels wait on one another: two ranks on one GPU would be
+        # two such kernels on one device, which nothing schedules together.
+        ids = [None] * self.world
+        dist.all_gather_object(ids, (socket.gethostname(), _device_uuid(idx)), group=group)
+        if len(set(ids)) != self.world:
+            raise RuntimeError("chained sequence sharding needs one distinct GPU per rank")
+        if len({h for h, _ in ids}) != 1:
+            raise RuntimeError("chained sequence sharding needs all ranks on one node")
+        with torch.cuda.device(idx):
+            mb = ctypes.c_void_p()
+            _lib.check(self.lib.fpscan_link_create(rows, depth, ctypes.byref(mb)),
+                       "fpscan_link_create")
+            self.local = mb.value
+            h = ctypes.create_string_buffer(64)
+            _lib.check(self.lib.fpscan_link_ipc_handle(self.local, h), "fpscan_link_ipc_handle")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, h.raw, group=group)
+            self.prev = self._open(handles[self.rank - 1]) if self.rank > 0 else None
+            self.next = self._open(handles[self.rank + 1]) if self.rank < self.world - 1 else None
+        self.device_index = idx
+        self.fwd_epoch = 0
+        self.bwd_epoch = 0
+
+    def _open(self, handle: bytes) -> int:
+        p = ctypes.c_void_p()
+        _lib.check(self.lib.fpscan_link_open(ctypes.create_string_buffer(handle, 64),
+                                             ctypes.byref(p)), "fpscan_link_open")
+        return p.value
+
+    @staticmethod
+    def _bump(e: int) -> int:
+        e = (e + 1) & 0xFFFFFFFF
+        return e or 1
+
+    def next_fwd_epoch(self) -> int:
+        self.fwd_epoch = self._bump(self.fwd_epoch)
+        return self.fwd_epoch
+
+    def next_bwd_epoch(self) -> int:
+        self.bwd_epoch = self._bump(self.bwd_epoch)
+        return self.bwd_epoch
+
+    def close(self) -> None:
+        """Unmap the neighbours' mailboxes, then (after every rank has done
+        the same) free this one.  Collective."""
+        if self.local is None:
+            return
+        with torch.cuda.device(self.device_index):
+            torch.cuda.synchronize()
+            for p in (self.prev, self.next):
+                if p:
+                    self.lib.fpscan_link_close(p)
+            dist.barrier(group=self.group)
+            self.lib.fpscan_link_destroy(self.local)
+        self.local = self.prev = self.next = None
+
+
+def _device_uuid(idx: int) -> str:
+    props = torch.cuda.get_device_properties(idx)
+    return str(getattr(props, "uuid", idx))
+
+
+_chains: dict = {}
+
+
+def _chain_for(rows: int, device: torch.device, group) -> RankChain:
+    key = (id(group), rows, device.index)
+    ch = _chains.get(key)
+    if ch is None:
+        ch = _chains[key] = RankChain(rows, device, group)
+    return ch
+
+
+def chain_supported(tokens_local: torch.Tensor) -> bool:
+    """Whether the chained mode applies: CUDA tensors whose local seqlen
+    exceeds one chunk of the linked kernels (1024 fp32 / 2048 half elements
+    forward; 2048 / 4096 backward)."""
+    if not tokens_local.is_cuda:
+        return False
+    vec = 16 // tokens_local.element_size()
+    return tokens_local.shape[-1] > 256 * vec * 2
+
+
+class ChainedSeqShardedPScan(torch.autograd.Function):
+    """Sequence-sharded scan with the row carries handed rank to rank over
+    NVLink inside the scan kernels (no reduce pass, no collective)."""
+
+    @staticmethod
+    def forward(ctx, gates, tokens, chain):
+        rows, L = tokens.numel() // tokens.shape[-1], tokens.shape[-1]
+        code = DTYPE_CODES[tokens.dtype]
+        y = torch.empty_like(tokens)
+        y_init = (torch.empty(rows, dtype=torch.float32, device=tokens.device)
+                  if chain.prev else None)
+        e = chain.next_fwd_epoch()
+        with torch.cuda.device(tokens.device):
+            _lib.call("fpscan_shard_fwd_link", gates.data_ptr(), tokens.data_ptr(), y.data_ptr(),
+                      y_init.data_ptr() if y_init is not None else None, rows, L, code,
+                      chain.local, chain.prev, chain.next, e, chain.depth,
+                      torch.cuda.current_stream(tokens.device).cuda_stream)
+        ctx.save_for_backward(gates, y, y_init if y_init is not None else y.new_empty(0))
+        ctx.chain, ctx.has_init = chain, y_init is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        gates, y, y_init = ctx.saved_tensors
+        chain = ctx.chain
+        grad_out = grad_out.contiguous()
+        rows, L = grad_out.numel() // grad_out.shape[-1], grad_out.shape[-1]
+        dg = torch.empty_like(grad_out)
+        dt = torch.empty_like(grad_out)
+        e = chain.next_bwd_epoch()
+        with torch.cuda.device(grad_out.device):
+            _lib.call("fpscan_shard_bwd_link", gates.data_ptr(), y.data_ptr(), grad_out.data_ptr(),
+                      dg.data_ptr(), dt.data_ptr(), y_init.data_ptr() if ctx.has_init else None,
+                      rows, L, DTYPE_CODES[grad_out.dtype], chain.local, chain.prev, chain.next,
+                      e, chain.depth, torch.cuda.current_stream(grad_out.device).cuda_stream)
+        return dg, dt, None
+
+
 def seq_sharded_pscan(gates_local: torch.Tensor, tokens_local: torch.Tensor,
-                      group: Optional[dist.ProcessGroup] = None, ops=None) -> torch.Tensor:
+                      group: Optional[dist.ProcessGroup] = None, ops=None,
+                      mode: str = "auto") -> torch.Tensor:
     """Differentiable scan of this rank's sequence shard ``(batch, dim, L/world)``.
 
     Rank r must hold positions [r*L/world, (r+1)*L/world) of every row, all
-    ranks the same rows.  Collectives: one all-gather of 2*rows fp32 forward
-    and one backward.
+    ranks the same rows, and every rank must make the same calls in the same
+    order.  ``mode``: "allgather" -- reduce, one all-gather of 2*rows fp32
+    (NCCL), scan with the combined state, both directions; "chain" -- the
+    carries pass rank to rank inside the scan kernels over NVLink (one
+    distinct GPU per rank, one node, local seqlen above one chunk); "auto"
+    -- "chain" where it applies, else "allgather".
     """
+    if mode not in ("auto", "chain", "allgather"):
+        raise ValueError(f"mode must be 'auto', 'chain' or 'allgather' (got {mode!r})")
     if ops is None:
         ops = CudaOps()
     _validate_local(gates_local, tokens_local, isinstance(ops, CudaOps))
+    world = dist.get_world_size(group)
+    use_chain = (mode == "chain" or (mode == "auto" and isinstance(ops, CudaOps)
+                                     and world > 1 and chain_supported(tokens_local)))
+    if use_chain:
+        if not isinstance(ops, CudaOps) or not chain_supported(tokens_local) or world < 2:
+            raise RuntimeError("chained mode needs CUDA shards on 2+ ranks with a local seqlen "
+                               "above one chunk")
+        rows = tokens_local.numel() // tokens_local.shape[-1]
+        chain = _chain_for(rows, tokens_local.device, group)
+        return ChainedSeqShardedPScan.apply(gates_local, tokens_local, chain)
     return SeqShardedPScan.apply(gates_local, tokens_local, group, ops)

@@ -232,6 +232,52 @@ FPSCAN_API int fpscan_shard_bwd_scan(const void* gates, const void* y, const voi
 FPSCAN_API int fpscan_carry_combine(const float* gathered, int world, int rank, int64_t rows,
                          int reverse, float* out, void* stream);
 
+/*
+ * Chained sequence sharding over NVLink peer memory (no reference
+ * counterpart; the reference has no multi-GPU path).  Rank r holds positions
+ * [r*L/world, (r+1)*L/world) of every row; instead of reduce + all-gather +
+ * scan (fpscan_shard_*), each rank's scan waits for the state entering each
+ * row from rank r-1 and hands the row's final state to rank r+1 (backward:
+ * the reverse direction) through a per-rank "mailbox" that the neighbours
+ * map with CUDA IPC.  Ranks must be distinct GPUs of one node.  Every wait is
+ * bounded (2 s, then status bit 3 is set and 0 is used).
+ *
+ * fpscan_link_bytes / _create / _destroy: the mailbox (cudaMalloc'd once,
+ * zeroed; `depth` ring slots per direction, epochs counted per direction
+ * starting at 1, slot = epoch % depth).  _ipc_handle writes 64 bytes to
+ * share with the neighbours; _open / _close map / unmap a neighbour's.
+ */
+FPSCAN_API int64_t fpscan_link_bytes(int64_t rows, int depth);
+FPSCAN_API int fpscan_link_create(int64_t rows, int depth, void** mailbox);
+FPSCAN_API int fpscan_link_destroy(void* mailbox);
+FPSCAN_API int fpscan_link_ipc_handle(void* mailbox, void* handle);
+FPSCAN_API int fpscan_link_open(const void* handle, void** peer_mailbox);
+FPSCAN_API int fpscan_link_close(void* peer_mailbox);
+
+/*
+ * Forward scan of this rank's shard (rows x seqlen, local seqlen a power of
+ * two larger than one chunk): zero initial state on the first rank (prev ==
+ * NULL), otherwise the state from rank r-1 (also stored to init_record when
+ * it is not NULL: the backward needs it); each row's final state goes to
+ * rank r+1 unless next == NULL.
+ */
+FPSCAN_API int fpscan_shard_fwd_link(const void* gates, const void* tokens, void* out,
+                                     float* init_record, int64_t rows, int64_t seqlen, int dtype,
+                                     void* local, void* prev, void* next, uint32_t epoch,
+                                     int depth, void* stream);
+
+/*
+ * Fused backward of this rank's shard: the value entering each row's last
+ * element comes from rank r+1 (next != NULL), gates[0]*dtokens[0] of each
+ * row goes to rank r-1 (prev != NULL); y_prev = the forward's init_record
+ * (y of the previous shard's last element; NULL on the first rank).
+ */
+FPSCAN_API int fpscan_shard_bwd_link(const void* gates, const void* y, const void* grad_out,
+                                     void* dgates, void* dtokens, const float* y_prev,
+                                     int64_t rows, int64_t seqlen, int dtype, void* local,
+                                     void* prev, void* next, uint32_t epoch, int depth,
+                                     void* stream);
+
 /* Message of the last failed call on this thread ("" if none). */
 FPSCAN_API const char* fpscan_last_error(void);
 

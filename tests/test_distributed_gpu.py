@@ -43,18 +43,36 @@ def _worker(rank, world, port, q, mode, dtype_name):
         x = (torch.randn(b, d, L, generator=gen, device=dev) / L).to(dtype)
         w = torch.randn(b, d, L, generator=gen, device=dev).to(dtype)
         tol = 1e-5 if dtype == torch.float32 else 1e-2
-        if mode == "seq":
+        if mode.startswith("seq"):
             Lr = L // world
             sl = slice(rank * Lr, (rank + 1) * Lr)
             gl = g[..., sl].contiguous().requires_grad_()
             xl = x[..., sl].contiguous().requires_grad_()
-            y = seq_sharded_pscan(gl, xl)
-            dgl, dxl = torch.autograd.grad(y, (gl, xl), w[..., sl].contiguous())
             y64 = oracle.scan_f64(g.double().cpu().numpy(), x.double().cpu().numpy())
             dg64, dt64 = oracle.scan_bwd_f64(g.double().cpu().numpy(), y64, w.double().cpu().numpy())
-            errs = [oracle.normwise_error(y.detach().double().cpu().numpy(), y64[..., sl]),
-                    oracle.normwise_error(dxl.double().cpu().numpy(), dt64[..., sl]),
-                    oracle.normwise_error(dgl.double().cpu().numpy(), dg64[..., sl])]
+            if mode == "seq_multi":
+                # 6 chained forwards in flight (more than the 4 ring slots:
+                # the producer rank must wait for the consumer's acks), one
+                # backward through all of them, repeated twice
+                errs = []
+                for _ in range(2):
+                    ys = [seq_sharded_pscan(gl, xl * (k + 1), mode="chain") for k in range(6)]
+                    loss = sum((yk * w[..., sl]).sum() for yk in ys)
+                    dgl, dxl = torch.autograd.grad(loss, (gl, xl))
+                    errs += [oracle.normwise_error(ys[5].detach().double().cpu().numpy() / 6,
+                                                   y64[..., sl]),
+                             oracle.normwise_error(dxl.double().cpu().numpy() / 21, dt64[..., sl]),
+                             oracle.normwise_error(dgl.double().cpu().numpy() / 21,
+                                                   dg64[..., sl])]
+                from fpscan_b200 import _lib
+                errs.append(float(_lib.device_status()))  # 0: no wait gave up
+            else:
+                m = {"seq": "auto", "seq_chain": "chain", "seq_allgather": "allgather"}[mode]
+                y = seq_sharded_pscan(gl, xl, mode=m)
+                dgl, dxl = torch.autograd.grad(y, (gl, xl), w[..., sl].contiguous())
+                errs = [oracle.normwise_error(y.detach().double().cpu().numpy(), y64[..., sl]),
+                        oracle.normwise_error(dxl.double().cpu().numpy(), dt64[..., sl]),
+                        oracle.normwise_error(dgl.double().cpu().numpy(), dg64[..., sl])]
         else:
             gl, xl = local_channels(g, rank, world), local_channels(x, rank, world)
             yl = fp.pscan(gl.contiguous(), xl.contiguous())
@@ -91,6 +109,20 @@ needs2 = pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs"
 @pytest.mark.parametrize("dtype_name", ["float32", "bfloat16"])
 def test_seq_sharded_nccl_matches_oracle(dtype_name):
     _run("seq", dtype_name)
+
+
+@needs2
+@pytest.mark.parametrize("mode", ["seq_chain", "seq_allgather"])
+def test_seq_sharded_modes_match_oracle(mode):
+    """Chained (carries rank to rank over NVLink inside the kernels) and
+    all-gather (NCCL) sequence sharding, each forced."""
+    _run(mode, "float32")
+
+
+@needs2
+def test_seq_sharded_chain_ring_backpressure():
+    """More chained calls in flight than ring slots, twice over."""
+    _run("seq_multi", "float32")
 
 
 @needs2
