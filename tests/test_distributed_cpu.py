@@ -110,3 +110,21 @@ def test_seq_sharded_exchange_matches_full_sequence(world):
 def test_channel_sharding_reassembles_full_scan():
     for rank, errs, _ in _run(_chan_worker, 4):
         assert errs[0] == 0.0
+
+
+def test_chain_mode_selection_and_epochs():
+    """Host logic of the chained sequence-sharded mode that needs no GPU:
+    mode validation, when "auto" picks the chain, epoch counting (never 0,
+    wraps at 2^32).  The chain itself runs in tests/test_distributed_gpu.py
+    (2 GPUs, one process each)."""
+    import sys
+    sys.path.insert(0, REPO)
+    from fpscan_b200 import distributed as fd
+
+    x = torch.empty(1, 2, 8192)
+    assert not fd.chain_supported(x)  # CPU tensors never chain
+    with pytest.raises(ValueError):
+        fd.seq_sharded_pscan(x, x, mode="ring")
+    assert fd.RankChain._bump(0) == 1
+    assert fd.RankChain._bump(41) == 42
+    assert fd.RankChain._bump(0xFFFFFFFF) == 1  # 0 is reserved (mailbox words start at 0)
