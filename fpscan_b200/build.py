@@ -94,7 +94,47 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     return out_path
 
 
+# ---------------------------------------------------------------- torch binding
+BINDING_SRC = os.path.join(PKG_DIR, "binding", "ext.cpp")
+BINDING_PATH = os.path.join(PKG_DIR, "_ext.so")
+
+
+def build_binding(force: bool = False, verbose: bool = False) -> str:
+    """Compile fpscan_b200/_ext.so: the thin torch/pybind binding over the C
+    ABI (fast path of ops.py for the reference's entry points).  Host code
+    only (g++ against torch's headers); links libfpscan_b200.so by rpath."""
+    deps = [BINDING_SRC, LIB_PATH, os.path.join(REPO_DIR, "include", "fpscan_b200.h"), __file__]
+    if (not force and os.path.exists(BINDING_PATH)
+            and all(os.path.getmtime(d) <= os.path.getmtime(BINDING_PATH) for d in deps)):
+        return BINDING_PATH
+    import sysconfig
+
+    import torch
+
+    torch_lib = os.path.join(os.path.dirname(torch.__file__), "lib")
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    incs = [os.path.join(os.path.dirname(torch.__file__), "include"),
+            os.path.join(os.path.dirname(torch.__file__), "include", "torch", "csrc", "api",
+                         "include"),
+            os.path.join(cuda_home, "include"), sysconfig.get_paths()["include"]]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    with tempfile.TemporaryDirectory(prefix="fpscan_bind_") as tmp:
+        out = os.path.join(tmp, "_ext.so")
+        cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-w",
+               f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_ext",
+               "-DTORCH_API_INCLUDE_EXTENSION_H", *[f"-I{i}" for i in incs], BINDING_SRC,
+               "-o", out, f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+               "-ltorch_cuda", "-ltorch_python", f"-L{PKG_DIR}", "-lfpscan_b200",
+               "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+        os.replace(out, BINDING_PATH)
+    return BINDING_PATH
+
+
 if __name__ == "__main__":
     path = build(force="--force" in sys.argv, verbose="-v" in sys.argv,
                  ptxas_verbose="--ptxas" in sys.argv)
     print(path)
+    print(build_binding(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -210,7 +210,7 @@ static int scan_fwd_impl(const void* gates, const void* tokens, void* out, int64
   // 512 rows) one row per CTA at 4 CTAs/SM is faster: two vectors per thread.
   if (act == kActNone && !getenv("FPSCAN_B200_NV") && dtype == FPSCAN_F32 &&
       rows <= 4 * (int64_t)a.num_sms)
-    a.nv = 2;
+    a.nv = 2;  // (four vectors with direct loads at seqlen 4096 measured slower: 14.3 vs 12.3 us)
   a.act = act;
   return cuda_result(launch_fwd(a), "fpscan_scan_fwd launch");
 }

@@ -82,6 +82,14 @@ def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+# ---- compiled binding (fpscan_b200/_ext.so, built by build.build_binding):
+# the reference's entry points through a thin C++ layer over the same C ABI;
+# when it is absent the ctypes path below does the same work.
+try:
+    from . import _ext as _EXT
+except ImportError:  # not built: ctypes path
+    _EXT = None
+
 # ---- launch path.  A call's host cost is on the critical path whenever the
 # GPU waits for it (small tensors, back-to-back calls), so the common case
 # avoids torch.cuda.device / Stream objects: the raw current stream and the
@@ -158,6 +166,8 @@ def fullscan_forward(gates: torch.Tensor, tokens: torch.Tensor, out: torch.Tenso
     (csrc/main.cpp:10 -> warpscan_fwd): validates, scans into ``out``, returns it.
     Few-channel, long-sequence shapes go to the split-row kernel, which needs
     a small per-stream workspace (kept here)."""
+    if _EXT is not None:
+        return _EXT.fullscan_forward(gates, tokens, out, bool(reverse))
     if not (_fast_valid(gates, tokens) and out.shape == tokens.shape
             and out.dtype is tokens.dtype and out.device == tokens.device and out.is_contiguous()):
         validate(gates, tokens, out)
@@ -205,6 +215,10 @@ def scan_forward(gates: torch.Tensor, tokens: torch.Tensor, reverse: bool = Fals
     the last element of the result in scan order.  The reference has only
     the zero state.
     """
+    if initial_state is None and _EXT is not None:
+        if out is None:
+            return _EXT.scan_forward(gates, tokens, bool(reverse))
+        return _EXT.fullscan_forward(gates, tokens, out, bool(reverse))
     if not _fns:
         _lib.load()  # fail loudly before allocating if the library is missing
     if out is None:
@@ -224,6 +238,8 @@ def scan_backward(gates: torch.Tensor, y: torch.Tensor, grad_output: torch.Tenso
     """Fused gradient of ``y = scan_forward(gates, tokens)``: one launch
     returning ``(grad_gates, grad_tokens)``.  Equals the reference's
     PScan.backward composition (fpscan/ops.py:70-83)."""
+    if _EXT is not None:
+        return _EXT.scan_backward(gates, y, grad_output)
     if not (_fast_valid(gates, grad_output) and _fast_valid(gates, y)):
         validate(gates, grad_output)
         validate(gates, y)

@@ -585,3 +585,26 @@ def test_gated_scan_matches_unfused_composition():
     dz2, dt2 = torch.autograd.grad(y2, (z2, x2), go)
     for a, b in ((y, y2), (dt, dt2), (dz, dz2)):
         assert oracle.normwise_error(_np64(a), _np64(b)) <= 2e-2
+
+
+def test_binding_and_ctypes_paths_agree(monkeypatch):
+    """ops.py reaches the C ABI through the compiled binding (_ext.so) when it
+    is built and through ctypes otherwise; both launch the same kernels."""
+    from fpscan_b200 import ops
+    assert ops._EXT is not None, "fpscan_b200/_ext.so not built (python -m fpscan_b200.build)"
+    g, x = _make_inputs(3, 40, 4096, torch.bfloat16, seed=5)
+    go = torch.randn_like(x)
+    y1 = fpscan.scan_forward(g, x)
+    r1 = fpscan.scan_forward(g, x, reverse=True)
+    d1 = ops.scan_backward(g, y1, go)
+    g1, x1 = g[:, :1].contiguous(), x[:, :1].contiguous()  # 3 rows: the split-row path
+    s1 = fpscan.scan_forward(g1, x1)
+    monkeypatch.setattr(ops, "_EXT", None)
+    y2 = fpscan.scan_forward(g, x)
+    r2 = fpscan.scan_forward(g, x, reverse=True)
+    d2 = ops.scan_backward(g, y2, go)
+    s2 = fpscan.scan_forward(g1, x1)
+    for a, b in ((y1, y2), (r1, r2), (d1[0], d2[0]), (d1[1], d2[1]), (s1, s2)):
+        assert torch.equal(a, b)
+    with pytest.raises(RuntimeError):
+        fpscan.scan_forward(g[..., :100].contiguous(), x[..., :100].contiguous())
