@@ -103,7 +103,8 @@ def build_binding(force: bool = False, verbose: bool = False) -> str:
     """Compile fpscan_b200/_ext.so: the thin torch/pybind binding over the C
     ABI (fast path of ops.py for the reference's entry points).  Host code
     only (g++ against torch's headers); links libfpscan_b200.so by rpath."""
-    deps = [BINDING_SRC, LIB_PATH, os.path.join(REPO_DIR, "include", "fpscan_b200.h"), __file__]
+    # the library is linked by name (rpath): a rebuilt library needs no relink
+    deps = [BINDING_SRC, os.path.join(REPO_DIR, "include", "fpscan_b200.h"), __file__]
     if (not force and os.path.exists(BINDING_PATH)
             and all(os.path.getmtime(d) <= os.path.getmtime(BINDING_PATH) for d in deps)):
         return BINDING_PATH

@@ -125,6 +125,13 @@ def test_seq_sharded_chain_ring_backpressure():
     _run("seq_multi", "float32")
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("mode", ["seq_chain", "seq_multi"])
+def test_seq_sharded_chain_4_ranks(mode):
+    """The chain through two interior ranks (both links on each)."""
+    _run(mode, "float32", world=4)
+
+
 @needs2
 def test_channel_sharded_nccl_bit_identical():
     _run("chan", "bfloat16")
