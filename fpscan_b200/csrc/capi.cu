@@ -628,27 +628,25 @@ int fpscan_scan_bwd_cl(const void* gates, const void* y, const void* grad_out, v
 
 // ------------------------------------------------------------------ rank links
 // Mailbox of one rank (cudaMalloc'd once per (rows, depth); 256-byte aligned
-// regions, 4-byte words):
-//   fwd_val[depth][rows] fwd_flag[depth][rows]   forward values from rank r-1
-//   bwd_val[depth][rows] bwd_flag[depth][rows]   backward values from rank r+1
-//   fwd_ack[rows]   epochs of forward values rank r+1 has consumed
-//   bwd_ack[rows]   epochs of backward values rank r-1 has consumed
-//   zeros[rows]     never written
+// regions):
+//   fwd[depth][rows]  64-bit words (epoch << 32 | value) from rank r-1
+//   bwd[depth][rows]  64-bit words from rank r+1
+//   fwd_ack[rows]     u32: epochs of forward words rank r+1 has taken
+//   bwd_ack[rows]     u32: epochs of backward words rank r-1 has taken
+//   zeros[rows]       fp32, never written
 // A call with epoch e uses ring slot e % depth; epochs start at 1 and are
 // counted per direction, so a producer waits for ack >= e - depth.
 namespace {
 struct MailboxLayout {
-  int64_t fwd_val, fwd_flag, bwd_val, bwd_flag, fwd_ack, bwd_ack, zeros, total;
+  int64_t fwd, bwd, fwd_ack, bwd_ack, zeros, total;
 };
 MailboxLayout mailbox_layout(int64_t rows, int depth) {
   auto up = [](int64_t b) { return (b + 255) / 256 * 256; };
-  const int64_t ring = up((int64_t)depth * rows * 4), one = up(rows * 4);
+  const int64_t ring = up((int64_t)depth * rows * 8), one = up(rows * 4);
   MailboxLayout m;
-  m.fwd_val = 0;
-  m.fwd_flag = m.fwd_val + ring;
-  m.bwd_val = m.fwd_flag + ring;
-  m.bwd_flag = m.bwd_val + ring;
-  m.fwd_ack = m.bwd_flag + ring;
+  m.fwd = 0;
+  m.bwd = m.fwd + ring;
+  m.fwd_ack = m.bwd + ring;
   m.bwd_ack = m.fwd_ack + one;
   m.zeros = m.bwd_ack + one;
   m.total = m.zeros + one;
@@ -748,14 +746,12 @@ int fpscan_shard_fwd_link(const void* gates, const void* tokens, void* out, floa
   a.lk.epoch = epoch;
   a.lk.depth = (uint32_t)depth;
   if (prev) {
-    a.lk.in_val = at<float>(local, m.fwd_val) + slot;
-    a.lk.in_flag = at<uint32_t>(local, m.fwd_flag) + slot;
+    a.lk.in_word = at<uint64_t>(local, m.fwd) + slot;
     a.lk.ack_out = at<uint32_t>(prev, m.fwd_ack);
     a.lk.in_record = init_record;
   }
   if (next) {
-    a.lk.out_val = at<float>(next, m.fwd_val) + slot;
-    a.lk.out_flag = at<uint32_t>(next, m.fwd_flag) + slot;
+    a.lk.out_word = at<uint64_t>(next, m.fwd) + slot;
     a.lk.ack_in = at<uint32_t>(local, m.fwd_ack);
   }
   return cuda_result(launch_fwd(a), "fpscan_shard_fwd_link launch");
@@ -795,13 +791,11 @@ int fpscan_shard_bwd_link(const void* gates, const void* y, const void* grad_out
   a.lk.epoch = epoch;
   a.lk.depth = (uint32_t)depth;
   if (next) {
-    a.lk.in_val = at<float>(local, m.bwd_val) + slot;
-    a.lk.in_flag = at<uint32_t>(local, m.bwd_flag) + slot;
+    a.lk.in_word = at<uint64_t>(local, m.bwd) + slot;
     a.lk.ack_out = at<uint32_t>(next, m.bwd_ack);
   }
   if (prev) {
-    a.lk.out_val = at<float>(prev, m.bwd_val) + slot;
-    a.lk.out_flag = at<uint32_t>(prev, m.bwd_flag) + slot;
+    a.lk.out_word = at<uint64_t>(prev, m.bwd) + slot;
     a.lk.ack_in = at<uint32_t>(local, m.bwd_ack);
   }
   return cuda_result(launch_bwd(a), "fpscan_shard_bwd_link launch");

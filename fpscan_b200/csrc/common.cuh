@@ -126,36 +126,61 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // ---------------------------------------------------------------- rank links
 // Cross-GPU hand-off of per-row values over NVLink peer memory (chained
-// sequence sharding).  The producer stores the value and then releases the
-// row's flag (the epoch of the call) at system scope; the consumer acquires
-// the flag and reads the value bypassing L1.
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+// sequence sharding).  A value travels with its epoch in one 64-bit word
+// (epoch << 32 | float bits) written by one single-copy-atomic relaxed store,
+// so the consumer polls the word itself: no flag, no fence.  Acks (the epoch
+// a consumer has taken) are relaxed 32-bit stores issued after the value was
+// loaded and used.  Loads are issued early (a chunk's start) and completed
+// late, so a poll that finds the word ready costs no stall.
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys_u32(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
   return v;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ float ld_relaxed_sys(const float* p) {
-  float v;
-  asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_relaxed_sys(float* p, float v) {
-  asm volatile("st.relaxed.sys.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+__device__ __forceinline__ uint64_t link_word(float v, uint32_t epoch) {
+  return ((uint64_t)epoch << 32) | __float_as_uint(v);
 }
 
-// Wait (bounded, 2 s) until the epoch-tagged word at p reaches `epoch`
-// (wrap-safe comparison).  On timeout records kStatusLinkTimeout, returns false.
-__device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t epoch) {
-  if ((int)(ld_acquire_sys(p) - epoch) >= 0) return true;
+// Completes a poll of the link word at p begun with `first` (an earlier load
+// of p): re-polls until its epoch reaches `epoch` (wrap-safe), bounded by
+// 2 s, then returns the value (0 and kStatusLinkTimeout on timeout).
+__device__ __forceinline__ float link_take(const uint64_t* p, uint32_t epoch, uint64_t first) {
+  uint64_t w = first;
+  if ((int)((uint32_t)(w >> 32) - epoch) < 0) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 0;; ++it) {
+      w = ld_relaxed_sys_u64(p);
+      if ((int)((uint32_t)(w >> 32) - epoch) >= 0) break;
+      if ((it & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
+        atomicOr(&g_status, kStatusLinkTimeout);
+        return 0.f;
+      }
+    }
+  }
+  return __uint_as_float((uint32_t)w);
+}
+
+// Completes a wait, begun with `first`, for the 32-bit word at p to reach
+// `target` (wrap-safe); bounded like link_take.
+__device__ __forceinline__ void link_wait_ack(const uint32_t* p, uint32_t target, uint32_t first) {
+  if ((int)(first - target) >= 0) return;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 0;; ++it) {
-    if ((int)(ld_acquire_sys(p) - epoch) >= 0) return true;
+    if ((int)(ld_relaxed_sys_u32(p) - target) >= 0) return;
     if ((it & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
       atomicOr(&g_status, kStatusLinkTimeout);
-      return false;
+      return;
     }
   }
 }

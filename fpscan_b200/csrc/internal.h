@@ -19,18 +19,16 @@ inline int ilog2_host(int64_t v) {
 
 // Chained sequence sharding: per-row hand-off between neighbouring ranks
 // through peer-mapped memory (see fpscan_link_* in capi.cu for the layout).
-// in_*: values arriving from the upstream rank (local memory); ack_out: the
-// upstream rank's ack word per row (peer memory), set to the epoch once the
-// value is consumed.  out_*: the downstream rank's slot (peer memory);
-// ack_in: this rank's ack words written by the downstream rank.  The out
-// value of a row is written only after ack_in shows the slot's previous use
-// (epoch - depth) consumed.
+// in_word: values arriving from the upstream rank (local memory; 64-bit
+// words epoch << 32 | float bits); ack_out: the upstream rank's ack word per
+// row (peer memory), set to the epoch once the value is taken.  out_word:
+// the downstream rank's slot (peer memory); ack_in: this rank's ack words,
+// written by the downstream rank.  A row's out word is written only after
+// ack_in shows the slot's previous use (epoch - depth) taken.
 struct LinkParams {
-  const float* in_val = nullptr;
-  const uint32_t* in_flag = nullptr;
+  const uint64_t* in_word = nullptr;
   uint32_t* ack_out = nullptr;
-  float* out_val = nullptr;
-  uint32_t* out_flag = nullptr;
+  uint64_t* out_word = nullptr;
   const uint32_t* ack_in = nullptr;
   float* in_record = nullptr;  // optional: received values are also stored here
   uint32_t epoch = 0;

@@ -147,6 +147,16 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
     const bool grp_row_end = ((vstart + E) & Lmask) == 0;  // holds a row's last element
     const bool grp_row_first = (vstart & Lmask) == 0;      // holds a row's first element
 
+    // LINK: start the polls this chunk needs (completed after pass 1)
+    uint64_t link_pre = 0;
+    uint32_t ack_pre = 0;
+    if constexpr ((LINK & 1) != 0)
+      if (tid == 0 && multi && ((off + CH) & Lmask) == 0)
+        link_pre = ld_relaxed_sys_u64(p.lk.in_word + row0 + (off >> lg));
+    if constexpr ((LINK & 2) != 0)
+      if (valid && grp_row_first)
+        ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + row0 + (vstart >> lg));
+
     const bool ok = mbar_wait_bounded(&s_bar[s], phase);
 
     Vec16<T> gv[NV], gov[NV], yv[NV];
@@ -207,9 +217,8 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
     if constexpr ((LINK & 1) != 0) {
       if (tid == 0 && multi && (((off + CH) & Lmask) == 0)) {
         const int64_t lrow = row0 + (off >> lg);
-        wait_epoch(p.lk.in_flag + lrow, p.lk.epoch);
-        s_link[buf] = ld_relaxed_sys(p.lk.in_val + lrow);
-        st_release_sys(p.lk.ack_out + lrow, p.lk.epoch);  // the slot may be reused
+        s_link[buf] = link_take(p.lk.in_word + lrow, p.lk.epoch, link_pre);
+        st_relaxed_sys_u32(p.lk.ack_out + lrow, p.lk.epoch);  // the slot may be reused
       }
     }
 
@@ -275,9 +284,9 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
         if constexpr ((LINK & 2) != 0) {
           if (grp_row_first) {
             const float v = Elem<T>::load(gv[0].e[0]) * dt[E - 1];
-            wait_epoch(p.lk.ack_in + row, p.lk.epoch - p.lk.depth);  // slot's last use consumed
-            st_relaxed_sys(p.lk.out_val + row, v);
-            st_release_sys(p.lk.out_flag + row, p.lk.epoch);
+            // the slot's previous use (epoch - depth) must have been taken
+            link_wait_ack(p.lk.ack_in + row, p.lk.epoch - p.lk.depth, ack_pre);
+            st_relaxed_sys_u64(p.lk.out_word + row, link_word(v, p.lk.epoch));
           }
         }
       } else if (grp_row_first) {

@@ -144,6 +144,16 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     const int64_t cnt = min((int64_t)CH, n - off);
     const bool valid = ((int64_t)vi << LGE) < cnt;
 
+    // LINK: start the polls this chunk needs (completed after pass 1)
+    uint64_t link_pre = 0;
+    uint32_t ack_pre = 0;
+    if constexpr ((LINK & 1) != 0)
+      if (tid == 0 && multi && (off & Lmask) == 0)
+        link_pre = ld_relaxed_sys_u64(p.lk.in_word + row0 + (off >> lg));
+    if constexpr ((LINK & 2) != 0)
+      if (tid == 0 && ((off + CH) & Lmask) == 0)
+        ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + row0 + (off >> lg));
+
     const bool ok = DIRECT || mbar_wait_bounded(&s_bar[s], phase);
 
     float a[E], b[E];
@@ -197,11 +207,10 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     if constexpr ((LINK & 1) != 0) {
       if (tid == 0 && multi && ((off & Lmask) == 0)) {
         const int64_t lrow = row0 + (off >> lg);
-        wait_epoch(p.lk.in_flag + lrow, p.lk.epoch);
-        const float v = ld_relaxed_sys(p.lk.in_val + lrow);
-        st_release_sys(p.lk.ack_out + lrow, p.lk.epoch);  // the slot may be reused
+        const float v = link_take(p.lk.in_word + lrow, p.lk.epoch, link_pre);
         s_link[buf] = v;
         if (p.lk.in_record) p.lk.in_record[lrow] = v;
+        st_relaxed_sys_u32(p.lk.ack_out + lrow, p.lk.epoch);  // the slot may be reused
       }
     }
 
@@ -259,9 +268,9 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
       }
       if constexpr ((LINK & 2) != 0) {
         if (tid == 0 && ((off + CH) & Lmask) == 0) {
-          wait_epoch(p.lk.ack_in + row, p.lk.epoch - p.lk.depth);  // slot's last use consumed
-          st_relaxed_sys(p.lk.out_val + row, carry);
-          st_release_sys(p.lk.out_flag + row, p.lk.epoch);
+          // the slot's previous use (epoch - depth) must have been taken
+          link_wait_ack(p.lk.ack_in + row, p.lk.epoch - p.lk.depth, ack_pre);
+          st_relaxed_sys_u64(p.lk.out_word + row, link_word(carry, p.lk.epoch));
         }
       }
     } else if (HAS_CARRY_OUT && valid && seg_lane_t == tpr - 1) {
