@@ -201,7 +201,12 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     }
 
     float ta = a[E - 1], tb = b[E - 1], pa, pb;
-    warp_exclusive(ta, tb, lane, wwidth, pa, pb);
+    // Rows spanning whole chunks take the constant-width scans (no segment
+    // arithmetic); short rows are scanned in segments of `wwidth` lanes.
+    if (multi)
+      warp_exclusive(ta, tb, lane, 32, pa, pb);
+    else
+      warp_exclusive(ta, tb, lane, wwidth, pa, pb);
     const int buf = (int)(k & 1);
     if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
     if constexpr ((LINK & 1) != 0) {
@@ -225,7 +230,10 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     }
 
     float ca = 1.f, cb = 0.f;
-    if (seg_warps >= 2) compose_warp_totals(s_wt[buf], lane, warp, seg_warps, pa, pb, ca, cb);
+    if (multi)
+      compose_warp_totals(s_wt[buf], lane, warp, kWarps, pa, pb, ca, cb);
+    else if (seg_warps >= 2)
+      compose_warp_totals(s_wt[buf], lane, warp, seg_warps, pa, pb, ca, cb);
 
     // Does this chunk start its row (in processing order)?
     const bool row_start = multi ? (((REV ? off + CH : off) & Lmask) == 0) : true;
