@@ -652,7 +652,7 @@ def run_layout_table(args, kind):
                "larger_than_l2": 3 * n * s > 126e6}
         if kind == "channels_last":
             row["kernel"] = ("streaming" if fpscan_b200.ops._lib.load().fpscan_cl_workspace_bytes(
-                d0, d1, d2, ops.DTYPE_CODES[dtype], 0) <= 256 else "look-back")
+                d0, d1, d2, ops.DTYPE_CODES[dtype], 0) <= 256 else "segmented")
             if d1 & (d1 - 1) == 0 and 32 <= d1 <= 65536 and 3 * n * s < 20e9:
                 def recipe():
                     return fpscan_b200.scan_forward(g.mT.contiguous(), x.mT.contiguous()).mT.contiguous()

@@ -138,7 +138,6 @@ cudaError_t launch_bwd(const BwdArgs& a);
 cudaError_t launch_anylen(const AnyArgs& a);
 cudaError_t launch_cl(const ClArgs& a);
 int64_t cl_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim, int dtype, bool backward);
-bool cl_use_stream(int64_t batch, int64_t dim, int dtype);
 cudaError_t launch_carry_combine(const float* gathered, int world, int rank, int64_t rows,
                                  int reverse, float* out, cudaStream_t stream);
 

@@ -136,9 +136,9 @@ FPSCAN_API int fpscan_scan_bwd_anylen(const void* gates, const void* y, const vo
  * .mT.contiguous() around pscan.  Any seqlen >= 1; dim*itemsize must be a
  * multiple of 16.  Needs a workspace of fpscan_cl_workspace_bytes() bytes
  * (16-byte aligned; 256 bytes when batch*ceil(dim_vectors/8) >= 128, else
- * about 3% of one tensor; reused across calls ordered on one stream without
- * clearing; calls that may overlap need separate workspaces).  `out` may
- * equal gates or tokens.
+ * the per-segment maps of the few-column path: columns x segments x
+ * channels x 12 bytes, well under a megabyte for such shapes; calls that may
+ * overlap need separate workspaces).  `out` may equal gates or tokens.
  */
 FPSCAN_API int64_t fpscan_cl_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim,
                                              int dtype, int backward);

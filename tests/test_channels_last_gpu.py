@@ -67,8 +67,9 @@ def test_channels_last_fwd_rev_bwd(dtype, shape):
 
 
 @pytest.mark.parametrize("shape", [(1, 100003, 128), (1, 70000, 256), (4, 20000, 4)])
-def test_channels_last_long_lookback_chains(shape):
-    """Few columns, many segments: deep decoupled look-back chains."""
+def test_channels_last_few_columns_long(shape):
+    """Few columns, long sequences: the time axis is cut into segments
+    (reduce, compose, scan)."""
     dtype = torch.float32
     g, x, go = _inputs(shape, dtype, seed=shape[1])
     g64, x64 = _t64(g), _t64(x)
@@ -109,7 +110,7 @@ def test_channels_last_matches_transposed_pscan(dtype):
 def test_channels_last_in_place_repeat_and_errors():
     g, x, _ = _inputs((2, 300, 64), torch.float32, seed=1)
     ref = _from64(oracle.scan_f64(_t64(g), _t64(x)))
-    for _ in range(3):  # workspace reused across calls (epoch-tagged status)
+    for _ in range(3):  # workspace reused across calls
         _check(fpscan.scan_forward_channels_last(g, x), ref, torch.float32, "repeat")
     xi = x.clone()
     fpscan.scan_forward_channels_last(g, xi, out=xi)
@@ -145,11 +146,11 @@ print("ok")
 """
 
 
-@pytest.mark.parametrize("path", ["stream", "lookback"])
-def test_channels_last_both_kernels(path):
-    """The streaming (one CTA per column) and look-back (columns split in
-    time) kernels, each forced on the same cases in a fresh process (the
-    choice is read once per process)."""
+@pytest.mark.parametrize("path", ["stream", "split"])
+def test_channels_last_both_paths(path):
+    """One CTA per column and the segmented path (columns cut in time),
+    each forced on the same cases in a fresh process (the choice is read
+    once per process)."""
     import os
     import subprocess
     import sys
@@ -158,4 +159,23 @@ def test_channels_last_both_kernels(path):
     env = dict(os.environ, FPSCAN_B200_CL_PATH=path)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                        timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+def test_channels_last_first_backward_on_autograd_thread():
+    """The first channel-last launch of a process can come from autograd's
+    backward worker thread, where no CUDA call has bound a context yet (the
+    TMA descriptors are encoded against the current context): run it in a
+    fresh process where the backward is the first launch of its kernel."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = (f"import sys; sys.path.insert(0, {os.path.dirname(here)!r}); import torch\n"
+            "import fpscan_b200 as fp\n"
+            "g = torch.rand(2, 64, 128, device='cuda').requires_grad_()\n"
+            "x = torch.randn(2, 64, 128, device='cuda').requires_grad_()\n"
+            "y = fp.pscan_channels_last(g, x)\n"
+            "torch.autograd.grad(y.sum(), (g, x)); torch.cuda.synchronize(); print('ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]

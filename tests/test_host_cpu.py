@@ -157,10 +157,13 @@ def test_channels_last_validation_and_c_abi_checks():
     assert lib.fpscan_scan_fwd_cl(16, 16, 16, 1, 0, 8, 0, 0, 16, 1 << 20, None) == 1
     assert b"seqlen" in lib.fpscan_last_error()
     need = lib.fpscan_cl_workspace_bytes(2, 1000, 256, 2, 0)
-    # tiles = 2 batches * 1 column block * ceil(1000 / 32) segments (32 timesteps
-    # per tile by default), 3088-byte records
-    assert need == 256 + 2 * 1 * 32 * 3088
-    assert lib.fpscan_cl_workspace_bytes(2, 1000, 256, 2, 1) == 256 + 2 * 32 * 3088
+    # few columns (2 batches x 4 columns of 8 vectors): the segmented path sizes
+    # its per-segment maps for ceil(2 * SMs / columns) segments (148 SMs assumed
+    # without a GPU): columns x segments x 64 bf16 channels x (8 + 4) bytes
+    n = 8 * 37 * 64
+    assert need == (n * 8 + 255) // 256 * 256 + n * 4
+    assert lib.fpscan_cl_workspace_bytes(2, 1000, 256, 2, 1) == need
+    assert lib.fpscan_cl_workspace_bytes(16, 1000, 5120, 2, 0) == 256  # 1280 columns: no segments
     assert lib.fpscan_scan_fwd_cl(1 << 20, 2 << 20, 3 << 20, 2, 1000, 256, 2, 0, 4 << 20, need - 16,
                                   None) == 1
     assert b"workspace too small" in lib.fpscan_last_error()
