@@ -78,10 +78,6 @@ def validate_layout(gates: torch.Tensor, tokens: torch.Tensor,
             raise RuntimeError("out must be contiguous")
 
 
-def _stream_ptr(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
-
-
 # ---- compiled binding (fpscan_b200/_ext.so, built by build.build_binding):
 # the reference's entry points through a thin C++ layer over the same C ABI;
 # when it is absent the ctypes path below does the same work.

@@ -283,10 +283,11 @@ FPSCAN_API const char* fpscan_last_error(void);
 
 /* Synchronously read (and if `clear`, reset) the current device's status
  * word.  Bit 0: a kernel gave up a bounded wait on its own copies; bit 1: a
- * split-row or channel-last scan gave up waiting for a preceding segment;
- * bit 2: a channel-last tile found its shared-memory staging buffer
- * misaligned for TMA and skipped it.  Results of such a launch are not
- * valid.  0 = healthy. */
+ * split-row scan gave up waiting for a preceding segment; bit 2: a
+ * channel-last CTA found its shared-memory staging buffer misaligned for TMA
+ * and skipped its work; bit 3: a chained sequence-sharded scan gave up
+ * waiting for a neighbouring rank (fpscan_shard_*_link).  Results of such a
+ * launch are not valid.  0 = healthy. */
 FPSCAN_API int fpscan_device_status(unsigned* status, int clear);
 
 #ifdef __cplusplus
