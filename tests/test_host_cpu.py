@@ -176,3 +176,32 @@ def test_channels_last_validation_and_c_abi_checks():
     assert lib.fpscan_scan_fwd_cl(0, 0, 0, 0, 10, 256, 2, 0, 0, 0, None) == 0
     with pytest.raises(RuntimeError):
         ops.validate_channels_last(t, t)  # CPU tensors are rejected like the reference's
+
+
+def test_link_abi_checks_without_gpu():
+    """Chained sequence-sharding entry points: mailbox size and argument
+    checks (all before any CUDA call)."""
+    lib = _lib.load()
+    rows, depth = 1000, 4
+    ring = -(-depth * rows * 8 // 256) * 256
+    one = -(-rows * 4 // 256) * 256
+    assert lib.fpscan_link_bytes(rows, depth) == 2 * ring + 3 * one
+    assert lib.fpscan_link_bytes(0, depth) == 0 and lib.fpscan_link_bytes(rows, 0) == 0
+    mb = 1 << 20
+    # neither neighbour
+    assert lib.fpscan_shard_fwd_link(16, 16, 16, None, rows, 8192, 0, mb, None, None, 1, depth,
+                                     None) == 1
+    assert b"upstream or a downstream" in lib.fpscan_last_error()
+    # epoch 0 is reserved
+    assert lib.fpscan_shard_fwd_link(16, 16, 16, None, rows, 8192, 0, mb, mb, None, 0, depth,
+                                     None) == 1
+    assert b"epoch" in lib.fpscan_last_error()
+    # local seqlen must exceed one chunk and be a power of two
+    for L in (1024, 3000):
+        assert lib.fpscan_shard_fwd_link(16, 16, 16, None, rows, L, 0, mb, mb, None, 1, depth,
+                                         None) == 1
+        assert b"seqlen" in lib.fpscan_last_error()
+    # backward: y_prev required when there is an upstream rank
+    assert lib.fpscan_shard_bwd_link(16, 16, 16, 16, 16, None, rows, 8192, 0, mb, mb, None, 1,
+                                     depth, None) == 1
+    assert b"y_prev" in lib.fpscan_last_error()
