@@ -237,7 +237,7 @@ def run_reference(args, cfg):
         t0 = time.perf_counter()
         step(g, x, go)
         dt = time.perf_counter() - t0
-        if dt * 2 * (args.steps + args.warmup) > 120 or rows >= 8192:
+        if dt * 2 * (args.steps + args.warmup) > args.ref_budget_s or rows >= 8192:
             break
         rows *= 2
     g, x, go = make(rows)
@@ -687,6 +687,9 @@ def main():
     ap.add_argument("--seq-mode", choices=["auto", "chain", "allgather"], default="auto",
                     help="shard_seq: carry exchange (chain: rank to rank over NVLink inside the "
                          "kernels; allgather: reduce + NCCL all-gather + scan)")
+    ap.add_argument("--ref-budget-s", type=float, default=120.0,
+                    help="--impl reference: size the per-step row sample so the run takes "
+                         "about this many seconds")
     ap.add_argument("--max-shapes", type=int, default=None,
                     help="anylen / channels_last: only the first N shapes of the table")
     args = ap.parse_args()

@@ -205,3 +205,27 @@ def test_link_abi_checks_without_gpu():
     assert lib.fpscan_shard_bwd_link(16, 16, 16, 16, 16, None, rows, 8192, 0, mb, mb, None, 1,
                                      depth, None) == 1
     assert b"y_prev" in lib.fpscan_last_error()
+
+
+def test_bench_reference_arm_json_contract():
+    """`bench.py --impl reference` (the reference's CPU path; runs without a
+    GPU) prints one JSON line with the keys the benchmark contract names."""
+    import json
+    import subprocess
+    import sys
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(repo, "bench.py"), "--impl", "reference",
+                        "--steps", "1", "--warmup", "3", "--ref-budget-s", "2"],
+                       capture_output=True, text=True,
+                       timeout=600, cwd=repo)
+    assert r.returncode == 0, r.stderr[-3000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "impl", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["value"] > 0
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    assert d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["cores"] >= 1
