@@ -55,6 +55,53 @@ int num_sms_current() {
   return sms;
 }
 
+// Counters of the dynamic row-unit scheduling (UnitSched, internal.h): one
+// 32-bit word per launch, zero between launches (a launch's last claim
+// resets its word), so launches that may run at the same time must not
+// share one.  Live launches cycle through kRingSlots words per device (a word
+// comes back only after kRingSlots later launches on that device); launches
+// recorded into a CUDA graph keep a word of their own for good, since the
+// graph can be replayed at any time (static tiling once those run out).  The
+// words are a file-scope device array, zeroed when the module loads on each
+// device, so no call allocates or clears memory for them.
+constexpr uint32_t kRingSlots = 1u << 16, kGraphSlots = 1u << 16;
+__device__ unsigned g_unit_ctr[kRingSlots + kGraphSlots];
+
+struct SchedPool {
+  std::atomic<unsigned*> base{nullptr};
+  std::atomic<uint32_t> ring{0};
+  std::atomic<uint32_t> graph{0};
+};
+SchedPool g_sched[64];
+
+unsigned* sched_counter(cudaStream_t stream) {
+  static const bool off = getenv("FPSCAN_B200_STATIC_TILES") != nullptr;
+  if (off) return nullptr;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  SchedPool& pool = g_sched[dev];
+  unsigned* base = pool.base.load(std::memory_order_acquire);
+  if (base == nullptr) {
+    if (cs != cudaStreamCaptureStatusNone) return nullptr;  // resolve outside captures
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_unit_ctr) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    base = static_cast<unsigned*>(p);
+    pool.base.store(base, std::memory_order_release);
+  }
+  if (cs == cudaStreamCaptureStatusNone)
+    return base + pool.ring.fetch_add(1, std::memory_order_relaxed) % kRingSlots;
+  const uint32_t g = pool.graph.fetch_add(1, std::memory_order_relaxed);
+  return g < kGraphSlots ? base + kRingSlots + g : nullptr;
+}
+
 struct Span {
   const char* name;
   uintptr_t lo, hi;
@@ -212,6 +259,7 @@ static int scan_fwd_impl(const void* gates, const void* tokens, void* out, int64
       rows <= 4 * (int64_t)a.num_sms)
     a.nv = 2;  // (four vectors with direct loads at seqlen 4096 measured slower: 14.3 vs 12.3 us)
   a.act = act;
+  a.sched = sched_counter(a.stream);
   return cuda_result(launch_fwd(a), "fpscan_scan_fwd launch");
 }
 
@@ -298,6 +346,7 @@ static int scan_bwd_impl(const void* gates, const void* y, const void* grad_out,
             static_cast<cudaStream_t>(stream)};
   a.nv = tuned_nv_act(false, dtype, act);
   a.act = act;
+  a.sched = sched_counter(a.stream);
   return cuda_result(launch_bwd(a), "fpscan_scan_bwd launch");
 }
 
@@ -337,6 +386,7 @@ int fpscan_scan_fwd_init(const void* gates, const void* tokens, void* out, const
   FwdArgs a{gates, tokens, out, init, nullptr, nullptr, rows, seqlen, dtype, reverse ? 1 : 0,
             num_sms_current(), static_cast<cudaStream_t>(stream)};
   a.nv = tuned_nv(true, dtype);
+  a.sched = sched_counter(a.stream);
   return cuda_result(launch_fwd(a), "fpscan_scan_fwd_init launch");
 }
 
@@ -353,6 +403,7 @@ int fpscan_shard_fwd_reduce(const void* gates, const void* tokens, float* carry_
   FwdArgs a{gates, tokens, nullptr, nullptr, carry_a, carry_b, r, seqlen, dtype, 0,
             num_sms_current(), static_cast<cudaStream_t>(stream)};
   a.nv = tuned_nv(true, dtype);
+  a.sched = sched_counter(a.stream);
   return cuda_result(launch_fwd(a), "fpscan_shard_fwd_reduce launch");
 }
 
@@ -369,6 +420,7 @@ int fpscan_shard_fwd_scan(const void* gates, const void* tokens, void* out, cons
   FwdArgs a{gates, tokens, out, y_init, nullptr, nullptr, r, seqlen, dtype, 0,
             num_sms_current(), static_cast<cudaStream_t>(stream)};
   a.nv = tuned_nv(true, dtype);
+  a.sched = sched_counter(a.stream);
   return cuda_result(launch_fwd(a), "fpscan_shard_fwd_scan launch");
 }
 
@@ -385,6 +437,7 @@ int fpscan_shard_bwd_reduce(const void* gates, const void* grad_out, float* carr
             carry_b, r,       seqlen,   dtype,   num_sms_current(),
             static_cast<cudaStream_t>(stream)};
   a.nv = tuned_nv(false, dtype);
+  a.sched = sched_counter(a.stream);
   return cuda_result(launch_bwd(a), "fpscan_shard_bwd_reduce launch");
 }
 
@@ -405,6 +458,7 @@ int fpscan_shard_bwd_scan(const void* gates, const void* y, const void* grad_out
             nullptr, r, seqlen,   dtype,  num_sms_current(),
             static_cast<cudaStream_t>(stream)};
   a.nv = tuned_nv(false, dtype);
+  a.sched = sched_counter(a.stream);
   return cuda_result(launch_bwd(a), "fpscan_shard_bwd_scan launch");
 }
 

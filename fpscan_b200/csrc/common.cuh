@@ -78,6 +78,13 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+// Plain arrive (no transaction bytes): completes the barrier's phase by
+// itself (count 1).  Used to hand consumers an end-of-work marker through a
+// stage that receives no copy.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // Non-multicast 1-D bulk copy global -> shared, completing on `bar`.
 // Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,

@@ -35,6 +35,52 @@ struct LinkParams {
   uint32_t depth = 1;
 };
 
+// Row-unit scheduling of the streaming kernels (scan_fwd.cu, scan_bwd.cu).
+// Streaming kernels cut their rows into units of `upr` whole rows.  Statically
+// tiled, a one-wave grid finishes when its slowest CTA does, and CTAs of one
+// launch were measured to finish up to 2x apart on B200 (a plain 2-read /
+// 1-write stream: first CTA done at 625 us of 1283 us).  So CTA b takes unit b
+// first and then claims further units from a 32-bit counter in global memory
+// (one atomicAdd per unit, issued one unit ahead so its latency is hidden).
+// Each launch makes exactly `nunits` claims: one per unit beyond the first
+// wave plus one failing claim per CTA.  The claim that returns nunits - 1 is
+// therefore the launch's last atomic on the counter, and its owner resets
+// the word to 0 for the next launch on the same counter.  The host gives
+// concurrent launches different counters (capi.cu, sched_counter).
+struct UnitSched {
+  unsigned* ctr = nullptr;  // null: static tiling, unit b = CTA b's whole tile
+  int64_t upr = 1;                    // rows per unit
+  int64_t nunits = 0;
+  int64_t grid = 0;                   // CTAs to launch
+};
+
+// Units of at least kUnitChunks chunks (and whole rows); static tiling (one
+// unit of ceil(rows / slots) rows per CTA) when there is no counter or no
+// more units than resident CTAs.
+constexpr int64_t kUnitChunks = 4;
+inline UnitSched plan_units(int64_t rows, int64_t seqlen, int64_t chunk, int64_t slots,
+                            unsigned* ctr) {
+  UnitSched u;
+  if (ctr != nullptr) {
+    int64_t upr = kUnitChunks * chunk / seqlen;
+    if (upr < 1) upr = 1;
+    const int64_t nunits = (rows + upr - 1) / upr;
+    if (nunits > slots && nunits < (int64_t(1) << 31)) {
+      u.ctr = ctr;
+      u.upr = upr;
+      u.nunits = nunits;
+      u.grid = slots;
+      return u;
+    }
+  }
+  int64_t rpt = (rows + slots - 1) / slots;
+  if (rpt < 1) rpt = 1;
+  u.upr = rpt;
+  u.nunits = (rows + rpt - 1) / rpt;
+  u.grid = u.nunits;
+  return u;
+}
+
 struct FwdArgs {
   const void* gates;
   const void* tokens;
@@ -52,6 +98,7 @@ struct FwdArgs {
   int act = 0;          // gate activation applied on load (Act); plain scan only
   int link = 0;         // bit 0: init from link.in_*; bit 1: final state to link.out_*
   LinkParams lk;
+  unsigned* sched = nullptr;  // unit counter (dynamic scheduling); null: static tiles
 };
 
 struct BwdArgs {
@@ -72,6 +119,7 @@ struct BwdArgs {
   int act = 0;          // gate activation (Act): dgates becomes d/dz; plain backward only
   int link = 0;         // bit 0: addend from link.in_*; bit 1: carry to link.out_*
   LinkParams lk;
+  unsigned* sched = nullptr;  // unit counter (dynamic scheduling); null: static tiles
 };
 
 struct SplitArgs {

@@ -20,6 +20,7 @@
 // gates[0] * dtokens[0], the value the previous shard needs.
 #include "common.cuh"
 #include "internal.h"
+#include "sched.cuh"
 
 namespace fpscan {
 
@@ -46,7 +47,7 @@ struct BwdKParams {
   const float* y_prev;
   float* carry_b;
   int64_t rows;
-  int64_t rows_per_tile;
+  UnitSched us;  // rows per unit, units, counter (null: static, one unit per CTA)
   int lg;
   LinkParams lk;
 };
@@ -84,15 +85,24 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
   T* __restrict__ dgates = static_cast<T*>(p.dgates);
   T* __restrict__ dtok = static_cast<T*>(p.dtok);
 
+  __shared__ int64_t s_abs[S];  // per stage: the chunk's first element in the tensor ...
+  __shared__ int s_cnt[S];      // ... and its element count (0: end of work)
+  __shared__ ProdState s_ps;
+
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lg = p.lg;
   const int64_t Lmask = (int64_t(1) << lg) - 1;
-  const int64_t row0 = (int64_t)blockIdx.x * p.rows_per_tile;
-  const int64_t nrows = min(p.rows_per_tile, p.rows - row0);
-  if (nrows <= 0) return;
-  const int64_t base = row0 << lg;
-  const int64_t n = nrows << lg;
-  const int64_t nck = (n + CH - 1) >> LGCH;
+  if ((int64_t)blockIdx.x >= p.us.nunits) return;
+  // Units and chunk hand-over as in scan_fwd.cu; link variants (always
+  // statically tiled) compute their chunk positions in every thread.
+  constexpr bool LOCAL = LINK != 0;
+  int64_t base0 = 0, n0 = 0, nck0 = 0;
+  if constexpr (LOCAL) {
+    const int64_t r0 = (int64_t)blockIdx.x * p.us.upr;
+    base0 = r0 << lg;
+    n0 = min(p.us.upr, p.rows - r0) << lg;
+    nck0 = (n0 + CH - 1) >> LGCH;
+  }
 
   const bool multi = lg > LGCH;
   const int tpr = multi ? kThreads : 1 << (lg - LGE);
@@ -106,28 +116,45 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
   }
   __syncthreads();
 
-  int64_t issued = 0;
-  auto issue = [&](int64_t k) {
-    const int64_t mc = nck - 1 - k;  // reverse processing order
-    const int64_t off = mc << LGCH;
-    const int64_t cnt = min((int64_t)CH, n - off);
-    const uint32_t bytes = (uint32_t)(cnt * (int64_t)sizeof(T));
-    const uint32_t g_bytes = bytes + ((off + cnt < n) ? 16u : 0u);
-    const int s = (int)(k % S);
+  unsigned claim = 0;
+  auto issue_next = [&]() {
+    ProdState& ps = s_ps;
+    if (ps.done) return;
+    const int s = (int)(ps.issued % S);
+    ++ps.issued;
+    if (ps.unit >= p.us.nunits) {
+      ps.done = 1;
+      s_cnt[s] = 0;
+      mbar_arrive(&s_bar[s]);
+      return;
+    }
+    const int64_t off = (ps.nck - 1 - ps.k) << LGCH;  // reverse processing order
+    const int64_t abs = ps.base + off;
+    const int cnt = (int)min((int64_t)CH, ps.n - off);
+    const uint32_t bytes = (uint32_t)cnt * (uint32_t)sizeof(T);
+    // halos within the unit: the gate after the chunk, the y before it
+    const uint32_t g_bytes = bytes + ((off + cnt < ps.n) ? 16u : 0u);
     uint32_t y_bytes = 0;
     if (HAS_OUT) y_bytes = bytes + (off > 0 ? 16u : 0u);
+    s_abs[s] = abs;
+    s_cnt[s] = cnt;
     mbar_expect_tx(&s_bar[s], g_bytes + bytes + y_bytes);
-    bulk_g2s(s_g + s * GS, gates + base + off, g_bytes, &s_bar[s]);
-    bulk_g2s(s_go + s * SV, gout + base + off, bytes, &s_bar[s]);
+    bulk_g2s(s_g + s * GS, gates + abs, g_bytes, &s_bar[s]);
+    bulk_g2s(s_go + s * SV, gout + abs, bytes, &s_bar[s]);
     if (HAS_OUT) {
       if (off > 0)
-        bulk_g2s(s_y + s * YS, y + base + off - V, y_bytes, &s_bar[s]);
+        bulk_g2s(s_y + s * YS, y + abs - V, y_bytes, &s_bar[s]);
       else
-        bulk_g2s(s_y + s * YS + 1, y + base + off, y_bytes, &s_bar[s]);
+        bulk_g2s(s_y + s * YS + 1, y + abs, y_bytes, &s_bar[s]);
+    }
+    if (++ps.k == ps.nck) {
+      ps.k = 0;
+      prod_next_unit<CH>(ps, p.us, p.rows, lg, claim);
     }
   };
   if (tid == 0) {
-    for (; issued < min((int64_t)S, nck); ++issued) issue(issued);
+    prod_init<CH>(s_ps, p.us, p.rows, lg, claim);
+    for (int i = 0; i < S; ++i) issue_next();
   }
 
   const int vi = kThreads - 1 - tid;  // slot in NV-vector units, reverse order
@@ -138,26 +165,37 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
   uint32_t phase = 0;
   bool aborted = false;
 
-  for (; k < nck; ++k) {
-    const int64_t mc = nck - 1 - k;
-    const int64_t off = mc << LGCH;
-    const int64_t cnt = min((int64_t)CH, n - off);
-    const int64_t vstart = off + ((int64_t)vi << LGE);  // tile-relative first element
-    const bool valid = vstart - off < cnt;
-    const bool grp_row_end = ((vstart + E) & Lmask) == 0;  // holds a row's last element
-    const bool grp_row_first = (vstart & Lmask) == 0;      // holds a row's first element
+  for (;; ++k) {
+    int64_t abs = 0;
+    int cnt = 0;
+    if constexpr (LOCAL) {
+      if (k >= nck0) break;
+      const int64_t off = (nck0 - 1 - k) << LGCH;
+      abs = base0 + off;
+      cnt = (int)min((int64_t)CH, n0 - off);
+    }
 
     // LINK: start the polls this chunk needs (completed after pass 1)
     uint64_t link_pre = 0;
     uint32_t ack_pre = 0;
     if constexpr ((LINK & 1) != 0)
-      if (tid == 0 && multi && ((off + CH) & Lmask) == 0)
-        link_pre = ld_relaxed_sys_u64(p.lk.in_word + row0 + (off >> lg));
-    if constexpr ((LINK & 2) != 0)
-      if (valid && grp_row_first)
-        ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + row0 + (vstart >> lg));
+      if (tid == 0 && multi && ((abs + CH) & Lmask) == 0)
+        link_pre = ld_relaxed_sys_u64(p.lk.in_word + (abs >> lg));
+    if constexpr ((LINK & 2) != 0) {
+      const int64_t vs = abs + ((int64_t)vi << LGE);
+      if ((vi << LGE) < cnt && (vs & Lmask) == 0)
+        ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + (vs >> lg));
+    }
 
     const bool ok = mbar_wait_bounded(&s_bar[s], phase);
+    if constexpr (!LOCAL) {
+      abs = s_abs[s];
+      cnt = s_cnt[s];
+    }
+    const int64_t vstart = abs + ((int64_t)vi << LGE);  // thread's first element
+    const bool valid = (vi << LGE) < cnt;
+    const bool grp_row_end = ((vstart + E) & Lmask) == 0;  // holds a row's last element
+    const bool grp_row_first = (vstart & Lmask) == 0;      // holds a row's first element
 
     Vec16<T> gv[NV], gov[NV], yv[NV];
     float g_next = 1.f, y_before = 0.f;
@@ -215,8 +253,8 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
     const int buf = (int)(k & 1);
     if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
     if constexpr ((LINK & 1) != 0) {
-      if (tid == 0 && multi && (((off + CH) & Lmask) == 0)) {
-        const int64_t lrow = row0 + (off >> lg);
+      if (tid == 0 && multi && (((abs + CH) & Lmask) == 0)) {
+        const int64_t lrow = abs >> lg;
         s_link[buf] = link_take(p.lk.in_word + lrow, p.lk.epoch, link_pre);
         st_relaxed_sys_u32(p.lk.ack_out + lrow, p.lk.epoch);  // the slot may be reused
       }
@@ -226,16 +264,14 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
       aborted = true;
       break;
     }
-    if (tid == 0 && issued < nck) {
-      issue(issued);
-      ++issued;
-    }
+    if (cnt == 0) break;  // end-of-work marker
+    if (tid == 0) issue_next();
 
     float ca = 1.f, cb = 0.f;
     if (seg_warps >= 2) compose_warp_totals(s_wt[buf], lane, warp, seg_warps, pa, pb, ca, cb);
 
-    const bool row_start = multi ? (((off + CH) & Lmask) == 0) : true;  // processing order
-    const int64_t row = row0 + ((multi ? off : vstart) >> lg);
+    const bool row_start = multi ? (((abs + CH) & Lmask) == 0) : true;  // processing order
+    const int64_t row = (multi ? abs : vstart) >> lg;
     float state;
     bool skip_state = false;
     if (row_start) {
@@ -274,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
             f_dg[j] = dt[i] * yp * act_grad<ACT>(gj);
           }
         }
-        uint4* d1 = reinterpret_cast<uint4*>(dtok + base + off) + vi * NV;
-        uint4* d2 = reinterpret_cast<uint4*>(dgates + base + off) + vi * NV;
+        uint4* d1 = reinterpret_cast<uint4*>(dtok + abs) + vi * NV;
+        uint4* d2 = reinterpret_cast<uint4*>(dgates + abs) + vi * NV;
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
           d1[q] = pack_vec<T>(f_dt + q * V);
@@ -303,8 +339,10 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
   }
 
   if (aborted && tid == 0) {
-    for (int64_t kk = k; kk < issued; ++kk)
+    // in-flight copies land first; remaining claims keep the counter's reset
+    for (int64_t kk = k; kk < s_ps.issued; ++kk)
       mbar_wait_bounded(&s_bar[kk % S], (uint32_t)((kk / S) & 1));
+    prod_drain_claims<CH>(s_ps, p.us, p.rows, lg, claim);
   }
 }
 
@@ -328,12 +366,12 @@ static cudaError_t launch_bwd_t(const BwdArgs& a) {
     if (dev >= 0 && dev < 64) occ_cache[dev] = occ;
   }
   const int64_t slots = (int64_t)a.num_sms * occ;
-  int64_t rpt = (a.rows + slots - 1) / slots;
-  if (rpt < 1) rpt = 1;
-  const int64_t tiles = (a.rows + rpt - 1) / rpt;
+  constexpr int64_t kChunk = (int64_t)kThreads * Elem<T>::kVec * NV;
+  const UnitSched us =
+      plan_units(a.rows, a.seqlen, kChunk, slots, LINK != 0 ? nullptr : a.sched);
   BwdKParams p{a.gates, a.y, a.grad_out, a.dgates, a.dtokens, a.addend, a.y_prev, a.carry_b,
-               a.rows, rpt, ilog2_host(a.seqlen), a.lk};
-  kern<<<(unsigned)tiles, kThreads, smem, a.stream>>>(p);
+               a.rows, us, ilog2_host(a.seqlen), a.lk};
+  kern<<<(unsigned)us.grid, kThreads, smem, a.stream>>>(p);
   return cudaGetLastError();
 }
 

@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "sched.cuh"
 
 namespace fpscan {
 
@@ -51,8 +52,8 @@ struct FwdKParams {
   float* carry_a;
   float* carry_b;
   int64_t rows;
-  int64_t rows_per_tile;
-  int lg;  // log2(seqlen)
+  UnitSched us;  // rows per unit, units, counter (null: static, one unit per CTA)
+  int lg;        // log2(seqlen)
   LinkParams lk;
 };
 
@@ -85,6 +86,10 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
   __shared__ float2 s_wt[2][kWarps];
   __shared__ float s_link[2];  // LINK bit 0: the row's initial state, by chunk parity
 
+  __shared__ int64_t s_abs[S];  // per stage: the chunk's first element in the tensor ...
+  __shared__ int s_cnt[S];      // ... and its element count (0: end of work)
+  __shared__ ProdState s_ps;
+
   const T* __restrict__ gates = static_cast<const T*>(p.gates);
   const T* __restrict__ tokens = static_cast<const T*>(p.tokens);
   T* out = static_cast<T*>(p.out);
@@ -92,12 +97,20 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lg = p.lg;
   const int64_t Lmask = (int64_t(1) << lg) - 1;
-  const int64_t row0 = (int64_t)blockIdx.x * p.rows_per_tile;
-  const int64_t nrows = min(p.rows_per_tile, p.rows - row0);
-  if (nrows <= 0) return;
-  const int64_t base = row0 << lg;
-  const int64_t n = nrows << lg;
-  const int64_t nck = (n + CH - 1) >> LGCH;
+  if ((int64_t)blockIdx.x >= p.us.nunits) return;
+  // Units are flat streams of whole rows (chunks never straddle units, and a
+  // unit starts a row, so an element's position in its row is abs & Lmask).
+  // Chunk positions reach the consumers through s_abs / s_cnt, except in
+  // LOCAL variants (direct loads; links, which are always statically tiled),
+  // where every thread computes them from its CTA's one tile.
+  constexpr bool LOCAL = DIRECT || LINK != 0;
+  int64_t base0 = 0, n0 = 0, nck0 = 0;
+  if constexpr (LOCAL) {
+    const int64_t r0 = (int64_t)blockIdx.x * p.us.upr;
+    base0 = r0 << lg;
+    n0 = min(p.us.upr, p.rows - r0) << lg;
+    nck0 = (n0 + CH - 1) >> LGCH;
+  }
 
   const bool multi = lg > LGCH;                        // a row spans several chunks
   const int tpr = multi ? kThreads : 1 << (lg - LGE);  // threads per segment
@@ -113,20 +126,37 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     __syncthreads();
   }
 
-  // Thread 0 issues chunk loads; `issued` counts them.
-  int64_t issued = 0;
-  auto issue = [&](int64_t k) {
-    const int64_t mc = REV ? nck - 1 - k : k;
-    const int64_t off = mc << LGCH;
-    const int64_t cnt = min((int64_t)CH, n - off);
-    const uint32_t bytes = (uint32_t)(cnt * (int64_t)sizeof(T));
-    const int s = (int)(k % S);
+  // Thread 0 fills the stages in order; after the last chunk of the last
+  // unit it completes one more stage with no copy and count 0.
+  unsigned claim = 0;
+  auto issue_next = [&]() {
+    ProdState& ps = s_ps;
+    if (ps.done) return;
+    const int s = (int)(ps.issued % S);
+    ++ps.issued;
+    if (ps.unit >= p.us.nunits) {
+      ps.done = 1;
+      s_cnt[s] = 0;
+      mbar_arrive(&s_bar[s]);
+      return;
+    }
+    const int64_t off = (REV ? ps.nck - 1 - ps.k : ps.k) << LGCH;
+    const int64_t abs = ps.base + off;
+    const int cnt = (int)min((int64_t)CH, ps.n - off);
+    const uint32_t bytes = (uint32_t)cnt * (uint32_t)sizeof(T);
+    s_abs[s] = abs;
+    s_cnt[s] = cnt;
     mbar_expect_tx(&s_bar[s], 2u * bytes);
-    bulk_g2s(s_g[s], gates + base + off, bytes, &s_bar[s]);
-    bulk_g2s(s_x[s], tokens + base + off, bytes, &s_bar[s]);
+    bulk_g2s(s_g[s], gates + abs, bytes, &s_bar[s]);
+    bulk_g2s(s_x[s], tokens + abs, bytes, &s_bar[s]);
+    if (++ps.k == ps.nck) {
+      ps.k = 0;
+      prod_next_unit<CH>(ps, p.us, p.rows, lg, claim);
+    }
   };
   if (!DIRECT && tid == 0) {
-    for (; issued < min((int64_t)S, nck); ++issued) issue(issued);
+    prod_init<CH>(s_ps, p.us, p.rows, lg, claim);
+    for (int i = 0; i < S; ++i) issue_next();
   }
 
   const int vi = REV ? kThreads - 1 - tid : tid;  // thread's slot (in NV-vector units)
@@ -138,23 +168,32 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
   uint32_t phase = 0;
   bool aborted = false;
 
-  for (; k < nck; ++k) {
-    const int64_t mc = REV ? nck - 1 - k : k;
-    const int64_t off = mc << LGCH;
-    const int64_t cnt = min((int64_t)CH, n - off);
-    const bool valid = ((int64_t)vi << LGE) < cnt;
+  for (;; ++k) {
+    int64_t abs = 0;
+    int cnt = 0;
+    if constexpr (LOCAL) {
+      if (k >= nck0) break;
+      const int64_t off = (REV ? nck0 - 1 - k : k) << LGCH;
+      abs = base0 + off;
+      cnt = (int)min((int64_t)CH, n0 - off);
+    }
 
     // LINK: start the polls this chunk needs (completed after pass 1)
     uint64_t link_pre = 0;
     uint32_t ack_pre = 0;
     if constexpr ((LINK & 1) != 0)
-      if (tid == 0 && multi && (off & Lmask) == 0)
-        link_pre = ld_relaxed_sys_u64(p.lk.in_word + row0 + (off >> lg));
+      if (tid == 0 && multi && (abs & Lmask) == 0)
+        link_pre = ld_relaxed_sys_u64(p.lk.in_word + (abs >> lg));
     if constexpr ((LINK & 2) != 0)
-      if (tid == 0 && ((off + CH) & Lmask) == 0)
-        ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + row0 + (off >> lg));
+      if (tid == 0 && ((abs + CH) & Lmask) == 0)
+        ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + (abs >> lg));
 
     const bool ok = DIRECT || mbar_wait_bounded(&s_bar[s], phase);
+    if constexpr (!LOCAL) {
+      abs = s_abs[s];
+      cnt = s_cnt[s];
+    }
+    const bool valid = (vi << LGE) < cnt;
 
     float a[E], b[E];
     if (valid) {
@@ -162,8 +201,8 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
       {
         uint4 rg[NV], rx[NV];
         if (DIRECT) {
-          const uint4* gsrc = reinterpret_cast<const uint4*>(gates + base + off) + vi * NV;
-          const uint4* xsrc = reinterpret_cast<const uint4*>(tokens + base + off) + vi * NV;
+          const uint4* gsrc = reinterpret_cast<const uint4*>(gates + abs) + vi * NV;
+          const uint4* xsrc = reinterpret_cast<const uint4*>(tokens + abs) + vi * NV;
 #pragma unroll
           for (int q = 0; q < NV; ++q) {
             rg[q] = __ldg(gsrc + q);
@@ -210,8 +249,8 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     const int buf = (int)(k & 1);
     if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
     if constexpr ((LINK & 1) != 0) {
-      if (tid == 0 && multi && ((off & Lmask) == 0)) {
-        const int64_t lrow = row0 + (off >> lg);
+      if (tid == 0 && multi && ((abs & Lmask) == 0)) {
+        const int64_t lrow = abs >> lg;
         const float v = link_take(p.lk.in_word + lrow, p.lk.epoch, link_pre);
         s_link[buf] = v;
         if (p.lk.in_record) p.lk.in_record[lrow] = v;
@@ -223,11 +262,9 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
       aborted = true;
       break;
     }
+    if (cnt == 0) break;  // end-of-work marker
     // Every thread has consumed stage s: refill it.
-    if (!DIRECT && tid == 0 && issued < nck) {
-      issue(issued);
-      ++issued;
-    }
+    if (!DIRECT && tid == 0) issue_next();
 
     float ca = 1.f, cb = 0.f;
     if (multi)
@@ -236,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
       compose_warp_totals(s_wt[buf], lane, warp, seg_warps, pa, pb, ca, cb);
 
     // Does this chunk start its row (in processing order)?
-    const bool row_start = multi ? (((REV ? off + CH : off) & Lmask) == 0) : true;
-    const int64_t row = row0 + ((multi ? off : off + ((int64_t)vi << LGE)) >> lg);
+    const bool row_start = multi ? (((REV ? abs + CH : abs) & Lmask) == 0) : true;
+    const int64_t row = (multi ? abs : abs + ((int64_t)vi << LGE)) >> lg;
     float state;  // y just before this thread's first element
     bool skip_state = false;
     if (row_start) {
@@ -261,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
       float f[E];  // memory order
 #pragma unroll
       for (int i = 0; i < E; ++i) f[REV ? E - 1 - i : i] = yv[i];
-      uint4* dst = reinterpret_cast<uint4*>(out + base + off) + vi * NV;
+      uint4* dst = reinterpret_cast<uint4*>(out + abs) + vi * NV;
 #pragma unroll
       for (int q = 0; q < NV; ++q) dst[q] = pack_vec<T>(f + q * V);
     }
@@ -270,12 +307,12 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
       const float new_carry = (row_start && !HAS_INIT) ? cb : fmaf(ca, carry, cb);
       acc_a = (row_start ? 1.f : acc_a) * ca;
       carry = new_carry;
-      if (HAS_CARRY_OUT && tid == 0 && ((REV ? off : off + CH) & Lmask) == 0) {
+      if (HAS_CARRY_OUT && tid == 0 && ((REV ? abs : abs + CH) & Lmask) == 0) {
         p.carry_a[row] = acc_a;
         p.carry_b[row] = carry;
       }
       if constexpr ((LINK & 2) != 0) {
-        if (tid == 0 && ((off + CH) & Lmask) == 0) {
+        if (tid == 0 && ((abs + CH) & Lmask) == 0) {
           // the slot's previous use (epoch - depth) must have been taken
           link_wait_ack(p.lk.ack_in + row, p.lk.epoch - p.lk.depth, ack_pre);
           st_relaxed_sys_u64(p.lk.out_word + row, link_word(carry, p.lk.epoch));
@@ -294,14 +331,17 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
 
   if (aborted && tid == 0) {
     // Let copies already in flight land before the CTA's shared memory is
-    // released.
-    for (int64_t kk = k; kk < issued; ++kk)
+    // released, and make this CTA's remaining claims (its failing one
+    // included) so the counter is still reset by the launch's last claim.
+    for (int64_t kk = k; kk < s_ps.issued; ++kk)
       mbar_wait_bounded(&s_bar[kk % S], (uint32_t)((kk / S) & 1));
+    prod_drain_claims<CH>(s_ps, p.us, p.rows, lg, claim);
   }
 }
 
-// One wave of CTAs: tiles = SMs x resident CTAs per SM (queried once per
-// device and kernel), each a contiguous run of whole rows.
+// One wave of CTAs (SMs x resident CTAs per SM, queried once per device and
+// kernel).  With a unit counter and more units than CTAs, rows are handed out
+// in units (plan_units); otherwise each CTA streams one contiguous tile.
 template <typename T, int NV, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT,
           int ACT, bool DIRECT = false, int LINK = 0>
 static cudaError_t launch_fwd_t(const FwdArgs& a) {
@@ -321,20 +361,21 @@ static cudaError_t launch_fwd_t(const FwdArgs& a) {
     if (dev >= 0 && dev < 64) occ_cache[dev] = occ;
   }
   const int64_t slots = (int64_t)a.num_sms * occ;
-  int64_t rpt = (a.rows + slots - 1) / slots;
-  if (rpt < 1) rpt = 1;
+  constexpr int64_t kChunk = (int64_t)kThreads * Elem<T>::kVec * NV;
+  // Links keep static tiles (every rank must tile its rows alike); direct
+  // loads are for one-chunk tiles only.
+  const UnitSched us = plan_units(a.rows, a.seqlen, kChunk, slots,
+                                  (DIRECT || LINK != 0) ? nullptr : a.sched);
   // Plain scans whose every tile is a single chunk (one wave of small
   // tiles) run the direct-load variant.
   if constexpr (!DIRECT && LINK == 0 && HAS_OUT && !HAS_INIT && !HAS_CARRY_OUT &&
                 ACT == kActNone) {
-    constexpr int64_t kChunk = (int64_t)kThreads * Elem<T>::kVec * NV;
-    if (rpt * a.seqlen <= kChunk && !getenv("FPSCAN_B200_NO_DIRECT"))
+    if (us.ctr == nullptr && us.upr * a.seqlen <= kChunk && !getenv("FPSCAN_B200_NO_DIRECT"))
       return launch_fwd_t<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT, true>(a);
   }
-  const int64_t tiles = (a.rows + rpt - 1) / rpt;
-  FwdKParams p{a.gates, a.tokens, a.out, a.init, a.carry_a, a.carry_b, a.rows, rpt,
+  FwdKParams p{a.gates, a.tokens, a.out, a.init, a.carry_a, a.carry_b, a.rows, us,
                ilog2_host(a.seqlen), a.lk};
-  kern<<<(unsigned)tiles, kThreads, smem, a.stream>>>(p);
+  kern<<<(unsigned)us.grid, kThreads, smem, a.stream>>>(p);
   return cudaGetLastError();
 }
 
