@@ -168,22 +168,29 @@ int cuda_result(cudaError_t e, const char* what) {
   return ok();
 }
 
-// Vectors per thread per chunk.  2 (default) amortises the per-chunk scan and
-// barrier over twice the data; FPSCAN_B200_NV=1 / =4 select the one- and
-// (fp32 only) four-vector variants (a tuning knob read once per process).
-// Measured defaults on B200 (configs 4 and 5): the forward scan is fastest
-// with 1 vector per thread (more resident CTAs / a deeper ring), the fused
-// backward with 2.
-int tuned_nv(bool forward, int dtype) {
+// Vectors per thread per chunk (NV).  FPSCAN_B200_NV=1 / 2 / 4 (4: fp32 only,
+// other types use 2) overrides the choice below (a tuning knob read once per
+// process).  Measured on B200 with dynamic row-unit scheduling, L2 flushed
+// between calls:
+//   forward: 2 -- the per-chunk block scan and barrier are amortised over
+//     twice the data (bf16 8x2048x8192: 6342 vs 5839 GB/s with 1; fp32
+//     4x8192x8192: 6849 vs 6306; fp16 16x5120x2048: 6392 vs 5992); launches
+//     of at most 2^18 elements take 1 (fp32 2x256x512: 3.5 vs 5.0 us);
+//   backward: 16-bit types 1 (bf16 8x2048x8192: 6404 vs 6179 GB/s; fp16
+//     16x5120x2048: 6572 vs 6379); fp32 2 once rows exceed four per SM
+//     (4x8192x8192: 6845 vs 6755), else 1 (2x256x65536: 5086 vs 4130).
+int tuned_nv(bool forward, int dtype, int64_t rows, int64_t seqlen) {
   static const int env = [] {
     const char* v = getenv("FPSCAN_B200_NV");
     if (v && v[0] == '1') return 1;
     if (v && v[0] == '2') return 2;
-    if (v && v[0] == '4') return 4;  // fp32 only; other types use 2
+    if (v && v[0] == '4') return 4;
     return 0;
   }();
   if (env) return env;
-  return forward ? 1 : 2;
+  if (forward) return rows * seqlen <= (int64_t(1) << 18) ? 1 : 2;
+  if (dtype != FPSCAN_F32) return 1;
+  return rows > 4 * (int64_t)num_sms_current() ? 2 : 1;
 }
 
 // Gated kernels (activation fused), measured at BASELINE config 4 (bf16):
@@ -191,9 +198,9 @@ int tuned_nv(bool forward, int dtype) {
 // per element (5.75 TB/s vs 5.2 with one), the backward runs under a 2-CTA
 // register budget (5.6 TB/s; one vector: 5.1; two at the 3-CTA budget
 // spilled: 3.2).
-int tuned_nv_act(bool forward, int dtype, int act) {
+int tuned_nv_act(bool forward, int dtype, int act, int64_t rows, int64_t seqlen) {
   if (act == kActNone || dtype == FPSCAN_F32 || getenv("FPSCAN_B200_NV"))
-    return tuned_nv(forward, dtype);
+    return tuned_nv(forward, dtype, rows, seqlen);
   return 2;
 }
 
@@ -251,13 +258,7 @@ static int scan_fwd_impl(const void* gates, const void* tokens, void* out, int64
       return fail(FPSCAN_ERR_INVALID, "out partially overlaps %s", in->name);
   FwdArgs a{gates, tokens, out, nullptr, nullptr, nullptr, rows, seqlen, dtype,
             reverse ? 1 : 0, num_sms_current(), static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv_act(true, dtype, act);
-  // One vector per thread (8-deep ring, 3 CTAs/SM) is the fp32 choice when
-  // rows fill several waves (config 5: 32768 rows); with few rows (config 2:
-  // 512 rows) one row per CTA at 4 CTAs/SM is faster: two vectors per thread.
-  if (act == kActNone && !getenv("FPSCAN_B200_NV") && dtype == FPSCAN_F32 &&
-      rows <= 4 * (int64_t)a.num_sms)
-    a.nv = 2;  // (four vectors with direct loads at seqlen 4096 measured slower: 14.3 vs 12.3 us)
+  a.nv = tuned_nv_act(true, dtype, act, rows, seqlen);
   a.act = act;
   a.sched = sched_counter(a.stream);
   return cuda_result(launch_fwd(a), "fpscan_scan_fwd launch");
@@ -344,7 +345,7 @@ static int scan_bwd_impl(const void* gates, const void* y, const void* grad_out,
   BwdArgs a{gates,   y,       grad_out, dgates, dtokens, nullptr, nullptr,
             nullptr, rows,    seqlen,   dtype,  num_sms_current(),
             static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv_act(false, dtype, act);
+  a.nv = tuned_nv_act(false, dtype, act, rows, seqlen);
   a.act = act;
   a.sched = sched_counter(a.stream);
   return cuda_result(launch_bwd(a), "fpscan_scan_bwd launch");
@@ -385,7 +386,7 @@ int fpscan_scan_fwd_init(const void* gates, const void* tokens, void* out, const
       return fail(FPSCAN_ERR_INVALID, "out partially overlaps %s", in->name);
   FwdArgs a{gates, tokens, out, init, nullptr, nullptr, rows, seqlen, dtype, reverse ? 1 : 0,
             num_sms_current(), static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv(true, dtype);
+  a.nv = tuned_nv(true, dtype, rows, seqlen);
   a.sched = sched_counter(a.stream);
   return cuda_result(launch_fwd(a), "fpscan_scan_fwd_init launch");
 }
@@ -402,7 +403,7 @@ int fpscan_shard_fwd_reduce(const void* gates, const void* tokens, float* carry_
   if (!carry_a || !carry_b) return fail(FPSCAN_ERR_INVALID, "carry_a/carry_b is NULL");
   FwdArgs a{gates, tokens, nullptr, nullptr, carry_a, carry_b, r, seqlen, dtype, 0,
             num_sms_current(), static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv(true, dtype);
+  a.nv = tuned_nv(true, dtype, r, seqlen);
   a.sched = sched_counter(a.stream);
   return cuda_result(launch_fwd(a), "fpscan_shard_fwd_reduce launch");
 }
@@ -419,7 +420,7 @@ int fpscan_shard_fwd_scan(const void* gates, const void* tokens, void* out, cons
   if (!y_init) return fail(FPSCAN_ERR_INVALID, "y_init is NULL");
   FwdArgs a{gates, tokens, out, y_init, nullptr, nullptr, r, seqlen, dtype, 0,
             num_sms_current(), static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv(true, dtype);
+  a.nv = tuned_nv(true, dtype, r, seqlen);
   a.sched = sched_counter(a.stream);
   return cuda_result(launch_fwd(a), "fpscan_shard_fwd_scan launch");
 }
@@ -436,7 +437,7 @@ int fpscan_shard_bwd_reduce(const void* gates, const void* grad_out, float* carr
   BwdArgs a{gates,   nullptr, grad_out, nullptr, nullptr, nullptr, nullptr,
             carry_b, r,       seqlen,   dtype,   num_sms_current(),
             static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv(false, dtype);
+  a.nv = tuned_nv(false, dtype, r, seqlen);
   a.sched = sched_counter(a.stream);
   return cuda_result(launch_bwd(a), "fpscan_shard_bwd_reduce launch");
 }
@@ -457,7 +458,7 @@ int fpscan_shard_bwd_scan(const void* gates, const void* y, const void* grad_out
   BwdArgs a{gates,   y, grad_out, dgates, dtokens, addend, y_prev,
             nullptr, r, seqlen,   dtype,  num_sms_current(),
             static_cast<cudaStream_t>(stream)};
-  a.nv = tuned_nv(false, dtype);
+  a.nv = tuned_nv(false, dtype, r, seqlen);
   a.sched = sched_counter(a.stream);
   return cuda_result(launch_bwd(a), "fpscan_shard_bwd_scan launch");
 }
@@ -782,7 +783,7 @@ int fpscan_shard_fwd_link(const void* gates, const void* tokens, void* out, floa
   if (prev == nullptr && next == nullptr)
     return fail(FPSCAN_ERR_INVALID, "a linked scan needs an upstream or a downstream rank");
   if (epoch == 0) return fail(FPSCAN_ERR_INVALID, "epoch 0 is reserved");
-  const int nv = tuned_nv(true, dtype) == 1 ? 1 : 2;
+  const int nv = 1;  // statically tiled: one vector per thread (measured at config 5)
   const int64_t chunk = (int64_t)kThreads * (16 / dtype_size(dtype)) * nv;
   if (!is_pow2(seqlen) || seqlen <= chunk || seqlen > kShardMaxL)
     return fail(FPSCAN_ERR_INVALID,

@@ -58,9 +58,7 @@ struct BwdKParams {
 // memory); bit 1 -- this rank's gates[0]*dtokens[0] of each row goes to the
 // upstream rank.  Link kernels always take y[-1] of each row from y_prev.
 template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY, int ACT, int LINK = 0>
-// Gated variants with two vectors per thread hold more live values: they get
-// a 2-CTA register budget (128) instead of spilling under the 3-CTA one.
-__global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : BwdCfg<NV>::kMinBlocks)
+__global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
     scan_bwd_kernel(const BwdKParams p) {
   constexpr int V = Elem<T>::kVec;
   constexpr int E = V * NV;
@@ -199,7 +197,10 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
 
     Vec16<T> gv[NV], gov[NV], yv[NV];
     float g_next = 1.f, y_before = 0.f;
-    float a[E], b[E];
+    // Two passes over the packed inputs: fold the thread's elements into its
+    // map (ta, tb) now, re-run the recurrence from the entering state after
+    // the block scan (no per-element arrays live across the barrier).
+    float ta = 1.f, tb = 0.f;
     {
       // Halo elements: gates[vstart+E] (first gate of the next slot) and
       // y[vstart-1] (last y of the previous slot).
@@ -232,23 +233,12 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
         const float g = (j == E - 1) ? g_next
                                       : act_fwd<ACT, T>(Elem<T>::load(gv[(j + 1) / V].e[(j + 1) % V]));
         const float x = Elem<T>::load(gov[j / V].e[j % V]);
-        if (i == 0) {
-          a[0] = g;
-          b[0] = x;
-        } else {
-          a[i] = a[i - 1] * g;
-          b[i] = fmaf(b[i - 1], g, x);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < E; ++i) {
-        a[i] = 1.f;
-        b[i] = 0.f;
+        ta = i == 0 ? g : ta * g;
+        tb = i == 0 ? x : fmaf(tb, g, x);
       }
     }
 
-    float ta = a[E - 1], tb = b[E - 1], pa, pb;
+    float pa, pb;
     warp_exclusive(ta, tb, lane, wwidth, pa, pb);
     const int buf = (int)(k & 1);
     if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
@@ -287,29 +277,36 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
       state = fmaf(pa, carry, pb);
     }
 
-    float dt[E];
+    // Pass 2, in processing order (element j = E-1-i at step i): dtokens by
+    // the recurrence from `state`, and dgates.  Each element's activated
+    // gate serves its own gradient factor and the next step's recurrence, so
+    // the activation is evaluated once per element here (once in pass 1).
+    float yp_first = y_before;
+    if (HAS_OUT && valid && grp_row_first)
+      yp_first = (HAS_CARRY || LINK != 0) ? p.y_prev[row] : 0.f;
+    float d = state;
+    float gcur = g_next;                     // activated gate of element j + 1
+    float f_dt[HAS_OUT ? E : 1], f_dg[HAS_OUT ? E : 1];  // memory order
 #pragma unroll
-    for (int i = 0; i < E; ++i) dt[i] = skip_state ? b[i] : fmaf(a[i], state, b[i]);
+    for (int i = 0; i < E; ++i) {
+      const int j = E - 1 - i;
+      const float x = Elem<T>::load(gov[j / V].e[j % V]);
+      d = (i == 0 && skip_state) ? x : fmaf(gcur, d, x);
+      const float gj = act_fwd<ACT, T>(Elem<T>::load(gv[j / V].e[j % V]));
+      if constexpr (HAS_OUT) {
+        const float yp = (j == 0) ? yp_first : Elem<T>::load(yv[(j - 1) / V].e[(j - 1) % V]);
+        f_dt[j] = d;
+        if constexpr (ACT == kActNone)
+          f_dg[j] = d * yp;
+        else
+          f_dg[j] = d * yp * act_grad<ACT>(gj);
+      }
+      gcur = gj;
+    }
+    // now d = dtokens of the group's first element, gcur = its (activated) gate
 
     if (valid) {
-      if (HAS_OUT) {
-        float yp_first = y_before;
-        if (grp_row_first) yp_first = (HAS_CARRY || LINK != 0) ? p.y_prev[row] : 0.f;
-        float f_dt[E], f_dg[E];  // memory order
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-          const int j = E - 1 - i;
-          const float yp = (j == 0) ? yp_first : Elem<T>::load(yv[(j - 1) / V].e[(j - 1) % V]);
-          f_dt[j] = dt[i];
-          if constexpr (ACT == kActNone) {
-            f_dg[j] = dt[i] * yp;
-          } else {
-            // recomputed rather than kept from the scan loop: E more live
-            // registers would spill at this kernel's register budget
-            const float gj = act_fwd<ACT, T>(Elem<T>::load(gv[j / V].e[j % V]));
-            f_dg[j] = dt[i] * yp * act_grad<ACT>(gj);
-          }
-        }
+      if constexpr (HAS_OUT) {
         uint4* d1 = reinterpret_cast<uint4*>(dtok + abs) + vi * NV;
         uint4* d2 = reinterpret_cast<uint4*>(dgates + abs) + vi * NV;
 #pragma unroll
@@ -319,14 +316,14 @@ __global__ void __launch_bounds__(kThreads, (ACT != kActNone && NV == 2) ? 2 : B
         }
         if constexpr ((LINK & 2) != 0) {
           if (grp_row_first) {
-            const float v = Elem<T>::load(gv[0].e[0]) * dt[E - 1];
+            const float v = gcur * d;
             // the slot's previous use (epoch - depth) must have been taken
             link_wait_ack(p.lk.ack_in + row, p.lk.epoch - p.lk.depth, ack_pre);
             st_relaxed_sys_u64(p.lk.out_word + row, link_word(v, p.lk.epoch));
           }
         }
       } else if (grp_row_first) {
-        p.carry_b[row] = Elem<T>::load(gv[0].e[0]) * dt[E - 1];  // plain scan only
+        p.carry_b[row] = gcur * d;  // plain scan only
       }
     }
 
