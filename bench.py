@@ -68,9 +68,9 @@ CONFIGS = {
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the backward
 # kernel, from one ncu capture (profiles/scan_fwd_bwd_bf16_cfg3_full.md) of
-# config 3 (134.2M elements: 1297.0 MB), scaled by the element count to the
+# config 3 (134.2M elements: 1294.0 MB), scaled by the element count to the
 # config-4 launch of each rank (traffic grows in proportion to the rows).
-_CFG3_BWD_TRAFFIC_PER_ELEM = 1297.0e6 / (8 * 2048 * 8192)
+_CFG3_BWD_TRAFFIC_PER_ELEM = 1294.0e6 / (8 * 2048 * 8192)
 
 
 def _peaks():
