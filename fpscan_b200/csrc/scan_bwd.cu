@@ -339,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
     // in-flight copies land first; remaining claims keep the counter's reset
     for (int64_t kk = k; kk < s_ps.issued; ++kk)
       mbar_wait_bounded(&s_bar[kk % S], (uint32_t)((kk / S) & 1));
-    prod_drain_claims<CH>(s_ps, p.us, p.rows, lg, claim);
+    drain_claims(s_ps.unit, p.us, claim);
   }
 }
 

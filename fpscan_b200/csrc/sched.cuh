@@ -44,29 +44,30 @@ __device__ __forceinline__ void prod_init(ProdState& ps, const UnitSched& us, in
   if (us.ctr != nullptr) claim = atomicAdd(us.ctr, 1u);
 }
 
-// Moves to the unit claimed earlier and claims the one after it.  The
-// launch's last claim (value nunits - 1) resets the counter.
+// Consumes the pending claim: returns the unit claimed earlier (>= nunits:
+// no more work) and, if it is one, claims the unit after it.  The launch's
+// last claim (value nunits - 1) resets the counter.  Static tiling (no
+// counter): no unit after the first.
+__device__ __forceinline__ int64_t take_claim(const UnitSched& us, unsigned& claim) {
+  if (us.ctr == nullptr) return us.nunits;
+  if ((int64_t)claim == us.nunits - 1) atomicExch(us.ctr, 0u);
+  const int64_t u = (int64_t)gridDim.x + (int64_t)claim;
+  if (u < us.nunits) claim = atomicAdd(us.ctr, 1u);
+  return u;
+}
+
+// Moves to the unit claimed earlier and claims the one after it.
 template <int CH>
 __device__ __forceinline__ void prod_next_unit(ProdState& ps, const UnitSched& us, int64_t rows,
                                                int lg, unsigned& claim) {
-  if (us.ctr == nullptr) {
-    ps.unit = us.nunits;
-    return;
-  }
-  if ((int64_t)claim == us.nunits - 1) atomicExch(us.ctr, 0u);
-  ps.unit = (int64_t)gridDim.x + (int64_t)claim;
-  if (ps.unit < us.nunits) {
-    prod_geom<CH>(ps, us, rows, lg);
-    claim = atomicAdd(us.ctr, 1u);
-  }
+  ps.unit = take_claim(us, claim);
+  if (ps.unit < us.nunits) prod_geom<CH>(ps, us, rows, lg);
 }
 
 // After an abort: makes the CTA's remaining claims (its failing one
 // included), so the counter is still reset by the launch's last claim.
-template <int CH>
-__device__ __forceinline__ void prod_drain_claims(ProdState& ps, const UnitSched& us,
-                                                  int64_t rows, int lg, unsigned& claim) {
-  while (us.ctr != nullptr && ps.unit < us.nunits) prod_next_unit<CH>(ps, us, rows, lg, claim);
+__device__ __forceinline__ void drain_claims(int64_t unit, const UnitSched& us, unsigned& claim) {
+  while (us.ctr != nullptr && unit < us.nunits) unit = take_claim(us, claim);
 }
 
 }  // namespace fpscan
