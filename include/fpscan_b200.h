@@ -11,7 +11,13 @@
  *     per-row carry buffers are always fp32.
  *   - Work is enqueued asynchronously on `stream` (a cudaStream_t; NULL is
  *     the legacy default stream).  The library never allocates device
- *     memory and keeps no per-call state; calls are re-entrant.
+ *     memory; calls are re-entrant.  The streaming kernels hand rows to
+ *     their CTAs through a counter word that each launch takes from a fixed
+ *     array in the library's own device memory (zero between launches), so
+ *     launches on different streams may run concurrently, and a launch
+ *     recorded into a CUDA graph keeps its word for every replay.  Make the
+ *     first call on a device outside any stream capture; launches captured
+ *     before it use static row tiles (same results, bit for bit).
  *   - Return 0 on success.  Non-zero: FPSCAN_ERR_INVALID (bad argument,
  *     nothing launched) or FPSCAN_ERR_CUDA (launch failed); the message is in
  *     fpscan_last_error() of the calling thread.
