@@ -12,8 +12,11 @@
 // carries one extra 16-byte vector after the chunk, the y stage one before it,
 // so no global re-reads are needed for the halos.
 //
-// Pipeline, tiling, segmentation of short rows and carry handling follow
-// scan_fwd.cu.  Optional per-row `addend` (value entering at the row's last
+// Pipeline, row-unit scheduling, segmentation of short rows and carry
+// handling follow scan_fwd.cu.  The thread-level scan is two-pass: a thread
+// folds its group into one map before the block scan and re-runs the
+// recurrence from the entering state after it, so no per-element values are
+// live across the barrier.  Optional per-row `addend` (value entering at the row's last
 // element, i.e. gates[L] * dtokens[L] of the next sequence shard) and
 // `y_prev` (y before the row's first element, from the previous shard) serve
 // the sequence-sharded mode; reduce mode (no outputs) emits per row

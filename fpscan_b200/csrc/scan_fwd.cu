@@ -3,11 +3,12 @@
 //
 // Replaces the reference kernel scan<> (csrc/full_scan/full_scan.cu:50-177)
 // with a different design:
-//   * one CTA streams a tile of whole consecutive rows, chunk by chunk, through
-//     a kStages-deep shared-memory ring filled by non-multicast cp.async.bulk
-//     copies completing on mbarriers; the grid is one wave (tiles =
-//     SMs x resident CTAs), so each CTA's pipeline runs across row boundaries
-//     without draining;
+//   * the grid is one wave (SMs x resident CTAs); each CTA streams units of
+//     whole consecutive rows -- its first unit by index, the rest claimed from
+//     a per-launch counter (sched.cuh), or one static tile -- chunk by chunk
+//     through a kStages-deep shared-memory ring filled by non-multicast
+//     cp.async.bulk copies completing on mbarriers, so its pipeline runs
+//     across row and unit boundaries without draining;
 //   * each thread owns NV consecutive 16-byte vectors of a chunk (4*NV fp32 or
 //     8*NV half values): in-register serial scan, warp-shuffle Hillis-Steele
 //     scan of the thread totals, then a lane-parallel scan of the
