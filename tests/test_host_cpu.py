@@ -229,3 +229,22 @@ def test_bench_reference_arm_json_contract():
     assert d["impl"] == "reference" and d["value"] > 0
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["cores"] >= 1
+
+
+def test_row_unit_planner(tmp_path):
+    """plan_units (csrc/internal.h): static tiles without a counter or with
+    fewer than two units per CTA slot, claimed units otherwise; every plan
+    covers all rows and fits one wave (tests/plan_units_check.cpp)."""
+    import shutil
+    import subprocess
+    here = os.path.dirname(os.path.abspath(__file__))
+    csrc = os.path.join(os.path.dirname(here), "fpscan_b200", "csrc")
+    cuda_inc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+    gxx = shutil.which("g++")
+    if gxx is None or not os.path.exists(os.path.join(cuda_inc, "cuda_runtime.h")):
+        pytest.skip("needs g++ and the CUDA headers")
+    exe = tmp_path / "plan_units_check"
+    subprocess.run([gxx, "-std=c++17", "-O1", "-I", csrc, "-I", cuda_inc,
+                    os.path.join(here, "plan_units_check.cpp"), "-o", str(exe)], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-3000:]
