@@ -195,9 +195,8 @@ int tuned_nv(bool forward, int dtype, int64_t rows, int64_t seqlen) {
 
 // Gated kernels (activation fused), measured at BASELINE config 4 (bf16):
 // two vectors per thread in both directions -- the forward does more work
-// per element (5.75 TB/s vs 5.2 with one), the backward runs under a 2-CTA
-// register budget (5.6 TB/s; one vector: 5.1; two at the 3-CTA budget
-// spilled: 3.2).
+// per element (6.84 TB/s vs 5.48 with one); the two-pass backward fits the
+// 3-CTA register budget at two vectors (5.98 TB/s vs 5.40 with one).
 int tuned_nv_act(bool forward, int dtype, int act, int64_t rows, int64_t seqlen) {
   if (act == kActNone || dtype == FPSCAN_F32 || getenv("FPSCAN_B200_NV"))
     return tuned_nv(forward, dtype, rows, seqlen);
