@@ -61,7 +61,9 @@ int num_sms_current() {
 // share one.  Live launches cycle through kRingSlots words per device (a word
 // comes back only after kRingSlots later launches on that device); launches
 // recorded into a CUDA graph keep a word of their own for good, since the
-// graph can be replayed at any time (static tiling once those run out).  The
+// graph can be replayed at any time (static tiling once those run out; two
+// executable instances of one captured graph share its words and must not
+// run at the same time).  The
 // words are a file-scope device array, zeroed when the module loads on each
 // device, so no call allocates or clears memory for them.
 constexpr uint32_t kRingSlots = 1u << 16, kGraphSlots = 1u << 16;
