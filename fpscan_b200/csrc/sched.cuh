@@ -8,6 +8,7 @@
 // is only paid where the value is used, one unit later.
 #pragma once
 
+#include "claim.h"
 #include "common.cuh"
 #include "internal.h"
 
@@ -32,6 +33,12 @@ __device__ __forceinline__ void prod_geom(ProdState& ps, const UnitSched& us, in
   ps.nck = (ps.n + CH - 1) / CH;
 }
 
+// The claim protocol (claim.h) on CUDA atomics.
+struct DeviceAtomics {
+  __device__ __forceinline__ unsigned add(unsigned* p) { return atomicAdd(p, 1u); }
+  __device__ __forceinline__ void reset(unsigned* p) { atomicExch(p, 0u); }
+};
+
 // CTA b starts with unit b; with a counter it also claims its next unit.
 template <int CH>
 __device__ __forceinline__ void prod_init(ProdState& ps, const UnitSched& us, int64_t rows,
@@ -41,19 +48,14 @@ __device__ __forceinline__ void prod_init(ProdState& ps, const UnitSched& us, in
   ps.issued = 0;
   ps.done = 0;
   prod_geom<CH>(ps, us, rows, lg);
-  if (us.ctr != nullptr) claim = atomicAdd(us.ctr, 1u);
+  DeviceAtomics at;
+  first_claim_t(us, claim, at);
 }
 
-// Consumes the pending claim: returns the unit claimed earlier (>= nunits:
-// no more work) and, if it is one, claims the unit after it.  The launch's
-// last claim (value nunits - 1) resets the counter.  Static tiling (no
-// counter): no unit after the first.
+// The unit claimed earlier (>= nunits: no more work); claims the next one.
 __device__ __forceinline__ int64_t take_claim(const UnitSched& us, unsigned& claim) {
-  if (us.ctr == nullptr) return us.nunits;
-  if ((int64_t)claim == us.nunits - 1) atomicExch(us.ctr, 0u);
-  const int64_t u = (int64_t)gridDim.x + (int64_t)claim;
-  if (u < us.nunits) claim = atomicAdd(us.ctr, 1u);
-  return u;
+  DeviceAtomics at;
+  return take_claim_t(us, claim, (int64_t)gridDim.x, at);
 }
 
 // Moves to the unit claimed earlier and claims the one after it.
@@ -64,10 +66,10 @@ __device__ __forceinline__ void prod_next_unit(ProdState& ps, const UnitSched& u
   if (ps.unit < us.nunits) prod_geom<CH>(ps, us, rows, lg);
 }
 
-// After an abort: makes the CTA's remaining claims (its failing one
-// included), so the counter is still reset by the launch's last claim.
+// After an abort: the CTA's remaining claims (claim.h, drain_claims_t).
 __device__ __forceinline__ void drain_claims(int64_t unit, const UnitSched& us, unsigned& claim) {
-  while (us.ctr != nullptr && unit < us.nunits) unit = take_claim(us, claim);
+  DeviceAtomics at;
+  drain_claims_t(unit, us, claim, (int64_t)gridDim.x, at);
 }
 
 }  // namespace fpscan

@@ -248,3 +248,22 @@ def test_row_unit_planner(tmp_path):
                     os.path.join(here, "plan_units_check.cpp"), "-o", str(exe)], check=True)
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-3000:]
+
+
+def test_row_unit_claim_protocol(tmp_path):
+    """The counter protocol of csrc/claim.h with CPU threads as CTAs
+    (tests/claim_protocol_check.cpp): every unit processed exactly once and
+    the counter word back at 0 after each launch, with aborting CTAs too."""
+    import shutil
+    import subprocess
+    here = os.path.dirname(os.path.abspath(__file__))
+    csrc = os.path.join(os.path.dirname(here), "fpscan_b200", "csrc")
+    cuda_inc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+    gxx = shutil.which("g++")
+    if gxx is None or not os.path.exists(os.path.join(cuda_inc, "cuda_runtime.h")):
+        pytest.skip("needs g++ and the CUDA headers")
+    exe = tmp_path / "claim_protocol_check"
+    subprocess.run([gxx, "-std=c++17", "-O1", "-pthread", "-I", csrc, "-I", cuda_inc,
+                    os.path.join(here, "claim_protocol_check.cpp"), "-o", str(exe)], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-3000:]
