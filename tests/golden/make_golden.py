@@ -1,7 +1,7 @@
 """Generate tests/golden/*.npz from the REFERENCE's own Python code.
 
-Run in a checkout that has the reference next to it:
-    python tests/golden/make_golden.py /root/reference
+Run with the path of a checkout of the reference:
+    python tests/golden/make_golden.py <reference checkout>
 It imports the reference's eval/baselines.py (sequential_scan,
 parallel_scan_torch) by path and evaluates, in float64 on the CPU:
 
