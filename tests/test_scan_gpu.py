@@ -467,7 +467,7 @@ def test_split_row_workspace_checks():
     assert lib.fpscan_scan_fwd_workspace_bytes(64, 1024, 4096, 0) == 0
 
 
-# ----------------------------------------------------------------- initial state (SURVEY 8f row 2)
+# ----------------------------------------------------------------- initial state
 def _scan_init_f64(g, x, h0, reverse=False):
     g, x = np.asarray(g, np.float64), np.asarray(x, np.float64)
     if reverse:
@@ -528,7 +528,7 @@ def test_initial_state_gradients(dtype, seqlen):
     check(h.grad, h64.grad.numpy(), dtype, "dh0")
 
 
-# ----------------------------------------------------------------- fused gate producers (SURVEY 8f row 4)
+# ----------------------------------------------------------------- fused gate producers
 _ACTS = {
     "sigmoid": (lambda z: 1 / (1 + np.exp(-z)), lambda g: g * (1 - g)),
     "exp_neg_softplus": (lambda z: np.exp(-np.logaddexp(0, z)), lambda g: -g * (1 - g)),
