@@ -16,12 +16,14 @@
 // library holds it until the process exits.  Its host-side name is only a
 // stand-in, so the device address is looked up with cudaGetSymbolAddress,
 // once per device, with that device current, by the first call on that
-// device (which also clears the array once).  Make that first call before
-// any stream capture.  All calls share the array and it keeps the last
-// call's contents: the tile counter is cleared by every call (an async
-// memset on the call's stream) and the status words carry a per-call epoch,
-// so nothing else must start at zero; calls that overlap on the GPU (two
-// streams, or two host threads) race on it and must not be issued.
+// device.  That set-up enqueues no GPU work (a __device__ array starts at
+// zero when the module loads), but make the first call on each device before
+// any stream capture all the same.  All calls share the array and it keeps
+// the last call's contents: the tile counter is cleared by every call (an
+// async memset on the call's own stream, ordered before its kernel) and the
+// status words carry a per-call epoch, so nothing else must start at zero;
+// calls that overlap on the GPU (two streams, or two host threads) race on
+// it and must not be issued.
 #include "../../include/fpscan_b200.h"
 #include "common.cuh"
 #include "internal.h"
@@ -49,8 +51,6 @@ cudaError_t scratch_for_current_device(void** addr) {
   if (g_scratch_addr[dev] == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    e = cudaMemset(p, 0, kNoAllocScratchBytes);
     if (e != cudaSuccess) return e;
     g_scratch_addr[dev] = p;
   }

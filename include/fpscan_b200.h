@@ -181,10 +181,14 @@ FPSCAN_API int fpscan_scan_fwd_init(const void* gates, const void* tokens, void*
  * results as fpscan_scan_fwd / fpscan_scan_fwd_ws; the scratch that
  * few-channel, long-sequence shapes need comes from a fixed array inside the
  * library (8,448 bytes per GPU, held until exit: at most 512 split
- * segments; larger needs are rejected with FPSCAN_ERR_INVALID).  The first
- * call on a device looks the array up and clears it (make it before any
- * stream capture).  Calls share the array: calls that overlap on the GPU
- * race and must not be issued.  Allocates nothing.
+ * segments; larger needs are rejected with FPSCAN_ERR_INVALID).  Whether a
+ * shape needs split segments, and how many, depends on the GPU's SM count
+ * and occupancy (fpscan_scan_fwd_workspace_bytes gives the need: the call
+ * accepts the shape when that is at most 8,448).  The first call on a device
+ * looks the array's address up (make it before any stream capture).  Every
+ * call clears the array's tile counter on its own stream.  Calls share the
+ * array: calls that overlap on the GPU race and must not be issued.
+ * Allocates nothing.
  * No counterpart in the reference.
  */
 FPSCAN_API int fpscan_scan_fwd_noalloc(const void* gates, const void* tokens, void* out,

@@ -6,18 +6,37 @@ place, never copied) together with oracle/ref_binding.cpp into
 flags (setup.py:36-47).  Needs the reference checkout, so it runs in the build
 container only; the built .so travels with the repository snapshot.
 Usage: python oracle/build_ref.py [REFERENCE_ROOT]
+
+The reference checkout is found from the argument, else the environment
+variable FPSCAN_REFERENCE_ROOT, else BASELINE.json's ``reference_path``.
 """
 from __future__ import annotations
 
+import json
 import os
 import sys
 
 ORACLE_DIR = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(ORACLE_DIR, "_ref")
-DEFAULT_REF = "/root/reference"
 
 
-def build(ref_root: str = DEFAULT_REF, verbose: bool = False) -> str | None:
+def reference_root() -> str | None:
+    """The reference checkout: $FPSCAN_REFERENCE_ROOT, else BASELINE.json's
+    reference_path; None when neither names an existing directory."""
+    root = os.environ.get("FPSCAN_REFERENCE_ROOT")
+    if not root:
+        try:
+            with open(os.path.join(os.path.dirname(ORACLE_DIR), "BASELINE.json")) as f:
+                root = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            root = None
+    return root if root and os.path.isdir(root) else None
+
+
+def build(ref_root: str | None = None, verbose: bool = False) -> str | None:
+    ref_root = ref_root or reference_root()
+    if ref_root is None:
+        return None
     src = os.path.join(ref_root, "csrc", "full_scan", "full_scan.cu")
     if not os.path.exists(src):
         return None
@@ -48,4 +67,4 @@ def build(ref_root: str = DEFAULT_REF, verbose: bool = False) -> str | None:
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else DEFAULT_REF, verbose=True))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None, verbose=True))

@@ -95,4 +95,11 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    from oracle.build_ref import reference_root
+
+    root = sys.argv[1] if len(sys.argv) > 1 else reference_root()
+    if root is None:
+        sys.exit("reference checkout not found: pass it as the argument or set "
+                 "FPSCAN_REFERENCE_ROOT")
+    main(root)

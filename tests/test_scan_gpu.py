@@ -608,3 +608,34 @@ def test_binding_and_ctypes_paths_agree(monkeypatch):
         assert torch.equal(a, b)
     with pytest.raises(RuntimeError):
         fpscan.scan_forward(g[..., :100].contiguous(), x[..., :100].contiguous())
+
+
+# ----------------------------------------------------------------- guard bands, workspace path
+@pytest.mark.parametrize("dtype,batch,dim,seqlen", [
+    (torch.float32, 2, 256, 65536), (torch.float32, 1, 1, 65536), (torch.float32, 3, 1, 32768),
+    (torch.float16, 1, 8, 65536), (torch.bfloat16, 1, 37, 65536), (torch.float32, 2, 3, 8192)])
+def test_ws_path_guarded(dtype, batch, dim, seqlen):
+    """fpscan_scan_fwd_ws (split rows with a decoupled look-back where the
+    shape takes it) writes its output into a guard-banded buffer: against
+    float64 in both directions, three calls in a row on one workspace, and no
+    element outside the output touched."""
+    from guard import guarded
+
+    lib = _lib.load()
+    code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[dtype]
+    gates, tokens = _make_inputs(batch, dim, seqlen, dtype, seed=seqlen + dim + batch)
+    need = lib.fpscan_scan_fwd_workspace_bytes(batch, dim, seqlen, code)
+    ws = torch.zeros(max(need, 16), dtype=torch.uint8, device=DEVICE)
+    stream = torch.cuda.current_stream().cuda_stream
+    for rev in (False, True):
+        ref = oracle.scan_f64(_np64(gates), _np64(tokens), reverse=rev)
+        for _ in range(3):
+            g = guarded(tokens.shape, dtype)
+            _lib.check(lib.fpscan_scan_fwd_ws(gates.data_ptr(), tokens.data_ptr(),
+                                              g.out.data_ptr(), batch, dim, seqlen, code,
+                                              int(rev), ws.data_ptr(), ws.numel(), stream),
+                       "fwd_ws")
+            g.check(f"fwd_ws rev={rev}")
+            _check(g.out, ref, dtype, f"fwd_ws rev={rev}")
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
