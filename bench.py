@@ -389,7 +389,7 @@ def run_fpscan(args, cfg):
     sweep = None
     if rank == 0 and world == 1 and not args.no_sweep:
         table, has_ref = _sweep_config2(device, 30, 3)
-        sweep = {"what": "BASELINE config 2: scan_forward fp32 2x256xL, p50 us and GB/s "
+        sweep = {"what": "BASELINE config 2: scan_forward fp32 2x256xL, us per call and GB/s "
                          "(3*N*4 bytes), cold inputs (rotating sets), this library beside the "
                          "reference's own kernel", "reference_kernel_timed": has_ref,
                  "table": table}
@@ -575,15 +575,17 @@ def _reference_extension():
         return None
 
 
-def _sweep_config2(device, iters, warmup, seqlens=None):
+def _sweep_config2(device, iters, warmup, seqlens=None, reps=5):
     """scan_forward, fp32, 2 x 256 channels, every seqlen
     32..65536, both directions, this library beside the reference's own
     kernel (fpscan._C from baseline/_ref, as eval/benchmark.py times it).
     Cold inputs: each call reads a different set of (gates, tokens, out)
     from a rotation whose sets together exceed 3x L2, so no flush kernel
-    (and no write-back of a flush buffer) lands in the timed call.  Each call
-    is timed alone with CUDA events, behind a short device-side sleep so the
-    host's launch cost is not in the interval; p50 of `iters` calls."""
+    (and no write-back of a flush buffer) lands in the timed calls.  `iters`
+    calls are queued behind a device-side sleep and run back to back between
+    two CUDA events (single calls of a few microseconds are below the event
+    timer's ~2 us resolution); the time per call is the median of `reps`
+    such runs."""
     import fpscan_b200
 
     ref = _reference_extension()
@@ -610,23 +612,26 @@ def _sweep_config2(device, iters, warmup, seqlens=None):
                     fn(g[i % nsets], x[i % nsets], o[i % nsets], rev)
                 torch.cuda.synchronize()
                 ts = []
-                for i in range(iters):
-                    k = i % nsets
-                    torch.cuda._sleep(20000)
+                for rep in range(reps):
+                    # a device-side sleep long enough for the host to queue
+                    # all `iters` calls, so they run back to back
+                    torch.cuda._sleep(iters * 40000)
                     a = torch.cuda.Event(enable_timing=True)
                     b = torch.cuda.Event(enable_timing=True)
                     a.record()
-                    fn(g[k], x[k], o[k], rev)
+                    for i in range(iters):
+                        k = (rep * iters + i) % nsets
+                        fn(g[k], x[k], o[k], rev)
                     b.record()
                     b.synchronize()
-                    ts.append(a.elapsed_time(b))
+                    ts.append(a.elapsed_time(b) / iters)
                 p50 = statistics.median(ts)
                 key = f"{name}_{'reverse' if rev else 'forward'}"
-                row[f"{key}_p50_us"] = round(p50 * 1e3, 2)
+                row[f"{key}_us"] = round(p50 * 1e3, 3)
                 row[f"{key}_gbs"] = round(3 * B * D * L * 4 / (p50 / 1e3) / 1e9, 1)
         if ref is not None:
             row["speedup_vs_reference_forward"] = round(
-                row["reference_forward_p50_us"] / row["fpscan_b200_forward_p50_us"], 3)
+                row["reference_forward_us"] / row["fpscan_b200_forward_us"], 3)
         table.append(row)
         del g, x, o
         torch.cuda.empty_cache()
@@ -651,7 +656,7 @@ def run_fwd_sweep(args, cfg):
     print(json.dumps({
         "metric": METRIC, "value": last["fpscan_b200_forward_gbs"], "unit": "GB/s", "n_gpus": 1,
         "steps": iters, "warmup": args.warmup,
-        "ms_per_step": last["fpscan_b200_forward_p50_us"] / 1e3, "higher_is_better": True,
+        "ms_per_step": last["fpscan_b200_forward_us"] / 1e3, "higher_is_better": True,
         "scaling": "none", "vs_baseline": None, "dtype": "float32",
         "data": "synthetic (seeded; BASELINE config 2)",
         "config": {"workload": "fwd_sweep: scan_forward fp32 batch=2 dim=256 seqlen=32..65536",

@@ -216,6 +216,14 @@ constexpr int64_t kShardMaxL = int64_t(1) << 24;
 
 }  // namespace
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("FPSCAN_B200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int set_error(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;

@@ -96,6 +96,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream serialization attribute may start while the previous kernel in its
+// stream is still running; pdl_wait() blocks until that kernel has completed
+// and its memory operations are visible (a no-op without the attribute).
+// Every thread calls it before its first global access.  pdl_launch_dependents()
+// lets the next such kernel start its own prologue early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

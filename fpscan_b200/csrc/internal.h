@@ -177,6 +177,27 @@ struct ClArgs {
   cudaStream_t stream;
 };
 
+// Launches `kern` on `stream` with programmatic stream serialization (the
+// kernel calls pdl_wait() before its first global access), so its prologue
+// overlaps the tail of the previous kernel in the stream.
+// FPSCAN_B200_PDL=0 launches without the attribute.
+bool pdl_enabled();
+template <typename K, typename P>
+cudaError_t launch_pdl(K kern, unsigned grid, unsigned threads, size_t smem, cudaStream_t stream,
+                       const P& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
 // Records `fmt` as this thread's fpscan_last_error() message; returns code.
 int set_error(int code, const char* fmt, ...);
 

@@ -116,6 +116,10 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
     fence_mbar_init();
   }
   __syncthreads();
+  // Everything above overlaps the previous kernel in the stream; from here
+  // on global memory is touched.
+  pdl_wait();
+  pdl_launch_dependents();
 
   unsigned claim = 0;
   auto issue_next = [&]() {
@@ -371,8 +375,7 @@ static cudaError_t launch_bwd_t(const BwdArgs& a) {
       plan_units(a.rows, a.seqlen, kChunk, slots, LINK != 0 ? nullptr : a.sched);
   BwdKParams p{a.gates, a.y, a.grad_out, a.dgates, a.dtokens, a.addend, a.y_prev, a.carry_b,
                a.rows, us, ilog2_host(a.seqlen), a.lk};
-  kern<<<(unsigned)us.grid, kThreads, smem, a.stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(kern, (unsigned)us.grid, kThreads, smem, a.stream, p);
 }
 
 template <typename T, bool HAS_OUT, bool HAS_CARRY, int ACT = kActNone>

@@ -126,6 +126,10 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     }
     __syncthreads();
   }
+  // Everything above overlaps the previous kernel in the stream; from here
+  // on global memory is touched.
+  pdl_wait();
+  pdl_launch_dependents();
 
   // Thread 0 fills the stages in order; after the last chunk of the last
   // unit it completes one more stage with no copy and count 0.
@@ -376,8 +380,7 @@ static cudaError_t launch_fwd_t(const FwdArgs& a) {
   }
   FwdKParams p{a.gates, a.tokens, a.out, a.init, a.carry_a, a.carry_b, a.rows, us,
                ilog2_host(a.seqlen), a.lk};
-  kern<<<(unsigned)us.grid, kThreads, smem, a.stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(kern, (unsigned)us.grid, kThreads, smem, a.stream, p);
 }
 
 template <typename T, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT, int ACT = kActNone>
