@@ -52,6 +52,8 @@ SIGNATURES = {
                               _vp, ctypes.c_uint32, _c_int, _vp],
     "fpscan_last_error": [],
     "fpscan_device_status": [ctypes.POINTER(ctypes.c_uint), _c_int],
+    "fpscan_status_snapshot": [_vp, _vp],
+    "fpscan_set_wait_limit_ns": [ctypes.c_uint64],
 }
 
 EXPECTED_ABI_VERSION = 1
@@ -107,3 +109,42 @@ def device_status(clear: bool = True) -> int:
     v = ctypes.c_uint(0)
     check(load().fpscan_device_status(ctypes.byref(v), 1 if clear else 0), "fpscan_device_status")
     return int(v.value)
+
+
+STATUS_BITS = {
+    1: "a kernel gave up waiting for its own copies to land",
+    2: "a split-row scan gave up waiting for a preceding segment (look-back)",
+    4: "a channel-last CTA found its staging buffer misaligned and skipped its work",
+    8: "a chained sequence-sharded scan gave up waiting for a neighbouring rank",
+}
+
+
+class DeviceStatusError(RuntimeError):
+    """A bounded device-side wait ran out: results of the launches since the
+    last check are not valid (the rows concerned hold NaN)."""
+
+
+def describe_status(status: int) -> str:
+    parts = [msg for bit, msg in STATUS_BITS.items() if status & bit]
+    rest = status & ~sum(STATUS_BITS)
+    if rest:
+        parts.append(f"unknown bits 0x{rest:x}")
+    return "; ".join(parts)
+
+
+def raise_on_status(status: int, where: str = "") -> None:
+    if status:
+        raise DeviceStatusError(f"fpscan device status 0x{status:x}{' (' + where + ')' if where else ''}: "
+                                f"{describe_status(status)}")
+
+
+def check_device_status(where: str = "") -> None:
+    """Synchronously read and clear the current device's status word; raise
+    DeviceStatusError (a RuntimeError) if a bounded wait ran out."""
+    raise_on_status(device_status(clear=True), where)
+
+
+def set_wait_limit(seconds: float) -> None:
+    """Limit of every bounded device-side wait on the current device
+    (default 2 s; 1 ms .. 600 s)."""
+    check(load().fpscan_set_wait_limit_ns(int(seconds * 1e9)), "fpscan_set_wait_limit_ns")

@@ -18,6 +18,12 @@
 namespace fpscan {
 
 __device__ unsigned int g_status = 0;
+__device__ unsigned long long g_wait_limit_ns = 2000000000ull;
+
+namespace {
+// Reads and clears the status word into *dst (device or mapped host memory).
+__global__ void status_take_kernel(unsigned* dst) { *dst = atomicExch(&g_status, 0u); }
+}  // namespace
 
 namespace {
 
@@ -482,6 +488,21 @@ int fpscan_carry_combine(const float* gathered, int world, int rank, int64_t row
   return cuda_result(launch_carry_combine(gathered, world, rank, rows, reverse ? 1 : 0, out,
                                           static_cast<cudaStream_t>(stream)),
                      "fpscan_carry_combine launch");
+}
+
+int fpscan_set_wait_limit_ns(uint64_t ns) {
+  if (ns < 1000000ull || ns > 600000000000ull)
+    return fail(FPSCAN_ERR_INVALID, "wait limit must be in [1 ms, 600 s] (got %llu ns)",
+                (unsigned long long)ns);
+  const unsigned long long v = ns;
+  return cuda_result(cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v)),
+                     "fpscan_set_wait_limit_ns");
+}
+
+int fpscan_status_snapshot(unsigned* dst, void* stream) {
+  if (!dst) return fail(FPSCAN_ERR_INVALID, "dst is NULL");
+  status_take_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(dst);
+  return cuda_result(cudaGetLastError(), "fpscan_status_snapshot launch");
 }
 
 int fpscan_device_status(unsigned* status, int clear) {

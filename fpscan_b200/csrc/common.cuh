@@ -34,6 +34,11 @@ enum : unsigned {
 
 extern __device__ unsigned int g_status;
 
+// Limit of every bounded wait, in ns of %globaltimer (per device; default
+// 2 s; fpscan_set_wait_limit_ns).  Read only once a wait did not complete
+// at its first try.
+extern __device__ unsigned long long g_wait_limit_ns;
+
 // ---------------------------------------------------------------- conversion
 template <typename T> struct Elem;
 template <> struct Elem<float> {
@@ -125,17 +130,17 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Wait for phase `parity` of `bar`, giving up after ~2 s of wall time.  A bulk
-// copy from valid device memory always completes, so the limit only guards
-// against a fault elsewhere turning into a hung GPU.  Returns false on
-// timeout (and records it in g_status).
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Wait for phase `parity` of `bar`, giving up after g_wait_limit_ns of wall
+// time.  A bulk copy from valid device memory always completes, so the limit
+// only guards against a fault elsewhere turning into a hung GPU.  Returns
+// false on timeout (and records it in g_status).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
+  const uint64_t limit = *(volatile unsigned long long*)&g_wait_limit_ns;
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
+    if ((it & 255u) == 255u && global_ns() - t0 > limit) {
       atomicOr(&g_status, kStatusWaitTimeout);
       return false;
     }
@@ -172,17 +177,20 @@ __device__ __forceinline__ uint64_t link_word(float v, uint32_t epoch) {
 
 // Completes a poll of the link word at p begun with `first` (an earlier load
 // of p): re-polls until its epoch reaches `epoch` (wrap-safe), bounded by
-// 2 s, then returns the value (0 and kStatusLinkTimeout on timeout).
+// g_wait_limit_ns, then returns the value.  On timeout it records
+// kStatusLinkTimeout and returns NaN, so the rows that needed the value come
+// out visibly wrong (NaN) rather than plausible.
 __device__ __forceinline__ float link_take(const uint64_t* p, uint32_t epoch, uint64_t first) {
   uint64_t w = first;
   if ((int)((uint32_t)(w >> 32) - epoch) < 0) {
     const uint64_t t0 = global_ns();
+    const uint64_t limit = *(volatile unsigned long long*)&g_wait_limit_ns;
     for (uint32_t it = 0;; ++it) {
       w = ld_relaxed_sys_u64(p);
       if ((int)((uint32_t)(w >> 32) - epoch) >= 0) break;
-      if ((it & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
+      if ((it & 63u) == 63u && global_ns() - t0 > limit) {
         atomicOr(&g_status, kStatusLinkTimeout);
-        return 0.f;
+        return __int_as_float(0x7fc00000);
       }
     }
   }
@@ -194,9 +202,10 @@ __device__ __forceinline__ float link_take(const uint64_t* p, uint32_t epoch, ui
 __device__ __forceinline__ void link_wait_ack(const uint32_t* p, uint32_t target, uint32_t first) {
   if ((int)(first - target) >= 0) return;
   const uint64_t t0 = global_ns();
+  const uint64_t limit = *(volatile unsigned long long*)&g_wait_limit_ns;
   for (uint32_t it = 0;; ++it) {
     if ((int)(ld_relaxed_sys_u32(p) - target) >= 0) return;
-    if ((it & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
+    if ((it & 63u) == 63u && global_ns() - t0 > limit) {
       atomicOr(&g_status, kStatusLinkTimeout);
       return;
     }

@@ -20,8 +20,9 @@
 //   [256, ..) one 16-byte status word per tile {A, B, B_incl, flag}.  Flags carry
 //             a per-launch epoch, so stale words from earlier launches are
 //             never mistaken for this launch's and need no clearing.
-// Look-back spins are bounded (2 s); on timeout the tile uses state 0 and
-// the device status word records kStatusLookbackTimeout.
+// Look-back spins are bounded (g_wait_limit_ns, 2 s by default); on timeout
+// the tile uses state NaN (its row comes out visibly wrong) and the device
+// status word records kStatusLookbackTimeout.
 #include "common.cuh"
 #include "internal.h"
 
@@ -190,14 +191,15 @@ __global__ void __launch_bounds__(kThreads, 3) scan_split_kernel(const SplitKPar
         while (true) {
           f = ld_acquire(&sj->flag);
           if ((f >> 1) == p.epoch) break;
-          if ((++spins & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) {
+          if ((++spins & 63u) == 0 &&
+              global_ns() - t0 > *(volatile unsigned long long*)&g_wait_limit_ns) {
             timed_out = true;
             break;
           }
         }
         if (timed_out) {
           atomicOr(&g_status, kStatusLookbackTimeout);
-          state_in = 0.f;
+          state_in = __int_as_float(0x7fc00000);  // NaN: the row is visibly wrong
           break;
         }
         if (f & 1u) {

@@ -30,7 +30,11 @@ applies): the reduce passes and the all-gathers disappear.  Each rank's scan
 kernel waits, row by row, for the state entering the row from rank r-1 and
 hands the row's final state to rank r+1 as soon as the row is done, through
 per-rank mailboxes mapped into the neighbours with CUDA IPC (stores and
-loads over NVLink; system-scope release / acquire flags, bounded waits).
+loads over NVLink; epoch-tagged words, bounded waits).  A wait that runs out
+(a neighbour more than the wait limit behind) makes the rows concerned NaN
+and sets a device status bit; every chained call queues a non-blocking read
+of that bit, and the next chained call (or ``check_chains()``) raises
+``DeviceStatusError``.
 The ranks run as a pipeline one row apart, each reading its shard once:
 forward 3*N*s and backward 5*N*s bytes per rank, as on one GPU.  The
 backward chain runs the other way; the state each rank received in the
@@ -57,6 +61,7 @@ import ctypes
 
 __all__ = [
     "RankChain",
+    "check_chains",
     "channel_slice",
     "channel_sharded_pscan",
     "seq_sharded_pscan",
@@ -234,6 +239,13 @@ class RankChain:
         self.device_index = idx
         self.fwd_epoch = 0
         self.bwd_epoch = 0
+        # Failure detection: after every linked launch a read-and-clear of
+        # the device status word is queued behind it (a 1-thread kernel into
+        # _status_dev, copied to pinned host memory, and an event); the host
+        # checks it once the event has completed -- at the next chained call
+        # without blocking, or in check(block=True).
+        self._status_dev = torch.zeros(1, dtype=torch.int32, device=device)
+        self._pending: list = []
 
     def _open(self, handle: bytes) -> int:
         p = ctypes.c_void_p()
@@ -253,6 +265,35 @@ class RankChain:
     def next_bwd_epoch(self) -> int:
         self.bwd_epoch = self._bump(self.bwd_epoch)
         return self.bwd_epoch
+
+    def after_launch(self, where: str) -> None:
+        """Queue the status check of the launch just issued on the current stream."""
+        stream = torch.cuda.current_stream(self.device_index)
+        host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        _lib.check(self.lib.fpscan_status_snapshot(self._status_dev.data_ptr(), stream.cuda_stream),
+                   "fpscan_status_snapshot")
+        host.copy_(self._status_dev, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self._pending.append((ev, host, where))
+
+    def check(self, block: bool = False) -> None:
+        """Raise DeviceStatusError if a queued status check shows that a
+        bounded wait ran out (a neighbouring rank fell behind by more than
+        the wait limit; the rows concerned hold NaN).  With block=False only
+        checks whose launches have completed are read."""
+        keep = []
+        for ev, host, where in self._pending:
+            if block:
+                ev.synchronize()
+            if block or ev.query():
+                status = int(host.item())
+                if status:
+                    self._pending = []
+                    _lib.raise_on_status(status, f"rank {self.rank}, {where}")
+            else:
+                keep.append((ev, host, where))
+        self._pending = keep
 
     def close(self) -> None:
         """Unmap the neighbours' mailboxes, then (after every rank has done
@@ -306,12 +347,14 @@ class ChainedSeqShardedPScan(torch.autograd.Function):
         y = torch.empty_like(tokens)
         y_init = (torch.empty(rows, dtype=torch.float32, device=tokens.device)
                   if chain.prev else None)
+        chain.check(block=False)
         e = chain.next_fwd_epoch()
         with torch.cuda.device(tokens.device):
             _lib.call("fpscan_shard_fwd_link", gates.data_ptr(), tokens.data_ptr(), y.data_ptr(),
                       y_init.data_ptr() if y_init is not None else None, rows, L, code,
                       chain.local, chain.prev, chain.next, e, chain.depth,
                       torch.cuda.current_stream(tokens.device).cuda_stream)
+            chain.after_launch(f"forward epoch {e}")
         ctx.save_for_backward(gates, y, y_init if y_init is not None else y.new_empty(0))
         ctx.chain, ctx.has_init = chain, y_init is not None
         return y
@@ -324,13 +367,23 @@ class ChainedSeqShardedPScan(torch.autograd.Function):
         rows, L = grad_out.numel() // grad_out.shape[-1], grad_out.shape[-1]
         dg = torch.empty_like(grad_out)
         dt = torch.empty_like(grad_out)
+        chain.check(block=False)
         e = chain.next_bwd_epoch()
         with torch.cuda.device(grad_out.device):
             _lib.call("fpscan_shard_bwd_link", gates.data_ptr(), y.data_ptr(), grad_out.data_ptr(),
                       dg.data_ptr(), dt.data_ptr(), y_init.data_ptr() if ctx.has_init else None,
                       rows, L, DTYPE_CODES[grad_out.dtype], chain.local, chain.prev, chain.next,
                       e, chain.depth, torch.cuda.current_stream(grad_out.device).cuda_stream)
+            chain.after_launch(f"backward epoch {e}")
         return dg, dt, None
+
+
+def check_chains(block: bool = True) -> None:
+    """Check every chain of this process (see RankChain.check): call it at a
+    point where the host may wait, e.g. before the optimizer step, to raise
+    for the step that failed rather than the next one."""
+    for ch in list(_chains.values()):
+        ch.check(block=block)
 
 
 def seq_sharded_pscan(gates_local: torch.Tensor, tokens_local: torch.Tensor,

@@ -300,6 +300,23 @@ FPSCAN_API const char* fpscan_last_error(void);
  * launch are not valid.  0 = healthy. */
 FPSCAN_API int fpscan_device_status(unsigned* status, int clear);
 
+/* Enqueue on `stream` a read-and-clear of the current device's status word
+ * into *dst (4 bytes of device memory, or of pinned host memory mapped into
+ * the device's address space), without synchronising: a caller checks the
+ * value once the stream has reached it (an event), so failures of a launch
+ * can be raised without stalling the host.  Allocates nothing.  The
+ * reference has no device-side waits and no counterpart. */
+FPSCAN_API int fpscan_status_snapshot(unsigned* dst, void* stream);
+
+/* Set the limit of every bounded device-side wait (copies landing, split-row
+ * look-back, chained neighbour ranks) on the current device, in ns, within
+ * [1 ms, 600 s]; default 2 s.  A wait that runs out sets its status bit and
+ * returns: a look-back or a neighbour value that never came is replaced by
+ * NaN, so the affected rows are visibly wrong.  Synchronous (a copy to a
+ * device symbol); set it while no scan runs.  No counterpart in the
+ * reference. */
+FPSCAN_API int fpscan_set_wait_limit_ns(uint64_t ns);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,6 +85,45 @@ def _chan_worker(rank, world, port, q):
         q.put((rank, None, traceback.format_exc()))
 
 
+def _dropout_worker(rank, world, port, q):
+    """Rank 1 never joins the exchange (it leaves after setting up the
+    process group); rank 0's sequence-sharded forward must end with an
+    error from its collective within the process group's timeout instead
+    of hanging or returning a result."""
+    try:
+        import datetime
+        import sys
+        import time
+        sys.path.insert(0, REPO)
+        sys.path.insert(0, os.path.join(REPO, "tests"))
+        from cpu_fake_ops import CpuOps
+        from fpscan_b200.distributed import seq_sharded_pscan
+
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}",
+                                rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=5))
+        if rank == 1:
+            q.put((rank, (0.0,), None))
+            q.close()
+            q.join_thread()
+            os._exit(0)  # leaves without a word: no barrier, no destroy
+        b, d, L = 2, 3, 64 * world
+        g, x, _ = _inputs(b, d, L, seed=3)
+        Lr = L // world
+        t0 = time.time()
+        try:
+            seq_sharded_pscan(g[..., :Lr].contiguous(), x[..., :Lr].contiguous(), ops=CpuOps())
+            outcome = 1.0  # returned a result: wrong
+        except (RuntimeError, dist.DistError):
+            outcome = 0.0 if time.time() - t0 < 60 else 1.0
+        q.put((rank, (outcome,), None))
+        q.close()
+        q.join_thread()
+        os._exit(0)
+    except Exception:
+        q.put((rank, None, traceback.format_exc()))
+
+
 def _run(worker, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -128,3 +167,8 @@ def test_chain_mode_selection_and_epochs():
     assert fd.RankChain._bump(0) == 1
     assert fd.RankChain._bump(41) == 42
     assert fd.RankChain._bump(0xFFFFFFFF) == 1  # 0 is reserved (mailbox words start at 0)
+
+
+def test_rank_that_never_joins_ends_the_exchange_with_an_error():
+    for rank, errs, _ in _run(_dropout_worker, 2):
+        assert errs[0] == 0.0, rank

@@ -32,6 +32,7 @@ def _worker(rank, world, port, q, mode, dtype_name):
         import oracle
         from fpscan_b200.distributed import local_channels, seq_sharded_pscan
 
+        os.environ["NCCL_NVLS_ENABLE"] = "0"  # no NVLink multicast objects in these tests
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
@@ -50,7 +51,31 @@ def _worker(rank, world, port, q, mode, dtype_name):
             xl = x[..., sl].contiguous().requires_grad_()
             y64 = oracle.scan_f64(g.double().cpu().numpy(), x.double().cpu().numpy())
             dg64, dt64 = oracle.scan_bwd_f64(g.double().cpu().numpy(), y64, w.double().cpu().numpy())
-            if mode == "seq_multi":
+            if mode == "seq_dropout":
+                # Failure injected on the host: after one healthy chained
+                # forward (which builds the chain), rank 0 skips the next
+                # call.  Rank 1's wait for rank 0's row states runs out
+                # (limit 0.2 s): its rows come out NaN and the chain's status
+                # check raises.  No kernel of either rank is left in flight.
+                from fpscan_b200 import _lib
+                from fpscan_b200.distributed import check_chains
+
+                y = seq_sharded_pscan(gl.detach(), xl.detach(), mode="chain")
+                errs = [oracle.normwise_error(y.double().cpu().numpy(), y64[..., sl])]
+                check_chains(block=True)
+                if rank == 1:
+                    fp.set_wait_limit(0.2)
+                    y = seq_sharded_pscan(gl.detach(), xl.detach(), mode="chain")
+                    raised = False
+                    try:
+                        check_chains(block=True)
+                    except fp.DeviceStatusError as exc:
+                        raised = "neighbouring rank" in str(exc)
+                    fp.set_wait_limit(2.0)
+                    errs += [0.0 if raised else 1.0,
+                             0.0 if bool(torch.isnan(y).all()) else 1.0,
+                             float(_lib.device_status())]  # cleared by the check
+            elif mode == "seq_multi":
                 # 6 chained forwards in flight (more than the 4 ring slots:
                 # the producer rank must wait for the consumer's acks), one
                 # backward through all of them, repeated twice
@@ -135,3 +160,11 @@ def test_seq_sharded_chain_4_ranks(mode):
 @needs2
 def test_channel_sharded_nccl_bit_identical():
     _run("chan", "bfloat16")
+
+
+@needs2
+def test_seq_sharded_chain_rank_dropout_raises():
+    """A rank that skips a chained call: its neighbour's bounded wait runs
+    out, its rows are NaN and the chain's status check raises
+    DeviceStatusError (instead of silently returning zeros)."""
+    _run("seq_dropout", "float32")
