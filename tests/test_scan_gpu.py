@@ -244,10 +244,23 @@ def test_agrees_with_reference_kernel(dtype, seqlen):
 
 
 @pytest.mark.skipif(_REF is None, reason="reference kernel not built (oracle/build_ref.py)")
-def test_backward_agrees_with_reference_composition():
-    gates, tokens = _make_inputs(4, 64, 8192, torch.bfloat16, seed=77)
+@pytest.mark.parametrize("dtype,shape,cfg3", [
+    (torch.bfloat16, (4, 64, 8192), False),
+    (torch.float16, (8, 2048, 8192), True),   # BASELINE config 3, fp16
+    (torch.bfloat16, (8, 2048, 8192), True),  # BASELINE config 3, bf16
+])
+def test_backward_agrees_with_reference_composition(dtype, shape, cfg3):
+    """The fused backward against the reference's own backward composition
+    (fpscan/ops.py:70-83: shift, reverse scan, multiply) run on the
+    reference's kernel; config-3 cases use that config's distributions."""
+    if cfg3:
+        gen = torch.Generator(device=DEVICE).manual_seed(3)
+        gates = torch.sigmoid(torch.randn(shape, generator=gen, device=DEVICE) + 2).to(dtype)
+        tokens = (torch.randn(shape, generator=gen, device=DEVICE) * 0.1).to(dtype)
+    else:
+        gates, tokens = _make_inputs(*shape, dtype, seed=77)
     gen = torch.Generator(device=DEVICE).manual_seed(78)
-    go = torch.randn(4, 64, 8192, generator=gen, device=DEVICE).to(torch.bfloat16)
+    go = torch.randn(shape, generator=gen, device=DEVICE).to(dtype)
 
     def ref_scan(g, x, rev):
         o = torch.empty_like(x)
@@ -283,7 +296,9 @@ def _sample_rows_check(gates, tokens, y, go=None, dg=None, dt=None, n=48, tol=1e
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_config3_mamba_like_fwd_bwd(dtype):
-    # batch 8, dim 2048, seqlen 8192, gates = sigmoid(N(2,1))
+    # batch 8, dim 2048, seqlen 8192, gates = sigmoid(N(2,1)).
+    # Every row (16384) of the forward and the fused backward against the
+    # float64 oracle, in blocks of rows.
     gen = torch.Generator(device=DEVICE).manual_seed(3)
     shape = (8, 2048, 8192)
     gates = torch.sigmoid(torch.randn(shape, generator=gen, device=DEVICE) + 2).to(dtype)
@@ -291,7 +306,17 @@ def test_config3_mamba_like_fwd_bwd(dtype):
     go = torch.randn(shape, generator=gen, device=DEVICE).to(dtype)
     y = fpscan.scan_forward(gates, tokens)
     dg, dt = fpscan.scan_backward(gates, y, go)
-    _sample_rows_check(gates, tokens, y, go, dg, dt)
+    L = shape[-1]
+    rows = gates.numel() // L
+    worst = [0.0, 0.0, 0.0]
+    for lo in range(0, rows, 2048):
+        blk = slice(lo, lo + 2048)
+        g64 = _np64(gates.view(rows, L)[blk])
+        y64 = oracle.scan_f64(g64, _np64(tokens.view(rows, L)[blk]))
+        dg64, dt64 = oracle.scan_bwd_f64(g64, y64, _np64(go.view(rows, L)[blk]))
+        for i, (got, ref) in enumerate(((y, y64), (dt, dt64), (dg, dg64))):
+            worst[i] = max(worst[i], oracle.normwise_error(_np64(got.view(rows, L)[blk]), ref))
+    assert max(worst) <= 1e-2, worst
 
 
 def test_config4_full_size_bf16():
@@ -312,16 +337,24 @@ def test_config4_full_size_bf16():
 
 
 def test_config5_2g_elements_fp32():
-    # BASELINE config 5 on one GPU: 4 x 8192 x 65536 fp32 = 2^31 elements
-    # (beyond 32-bit element offsets).  Sampled rows include the last ones.
+    # BASELINE config 5 on one GPU, forward and fused backward: 4 x 8192 x
+    # 65536 fp32 = 2^31 elements per tensor (beyond 32-bit element offsets,
+    # including the backward's halo offsets).  Sampled rows, plus the last two
+    # rows, against float64.
     gen = torch.Generator(device=DEVICE).manual_seed(5)
     shape = (4, 8192, 65536)
     gates = 0.999 + 0.001 * torch.rand(shape, generator=gen, device=DEVICE)
     tokens = torch.randn(shape, generator=gen, device=DEVICE) / 65536
+    go = torch.randn(shape, generator=gen, device=DEVICE)
     y = fpscan.scan_forward(gates, tokens)
-    _sample_rows_check(gates, tokens, y, tol=1e-5, seed=5)
-    last = oracle.scan_f64(_np64(gates[-1, -2:]), _np64(tokens[-1, -2:]))
+    dg, dt = fpscan.scan_backward(gates, y, go)
+    _sample_rows_check(gates, tokens, y, go, dg, dt, tol=1e-5, seed=5)
+    g64, x64 = _np64(gates[-1, -2:]), _np64(tokens[-1, -2:])
+    last = oracle.scan_f64(g64, x64)
     assert oracle.normwise_error(_np64(y[-1, -2:]), last) <= 1e-5
+    dg64, dt64 = oracle.scan_bwd_f64(g64, last, _np64(go[-1, -2:]))
+    assert oracle.normwise_error(_np64(dt[-1, -2:]), dt64) <= 1e-5
+    assert oracle.normwise_error(_np64(dg[-1, -2:]), dg64) <= 1e-5
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
