@@ -35,6 +35,9 @@ SIGNATURES = {
     "fpscan_scan_bwd_cl": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp, _c_i64,
                            _vp],
     "fpscan_scan_bwd": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp],
+    "fpscan_scan_bwd_workspace_bytes": [_c_i64, _c_i64, _c_i64, _c_int],
+    "fpscan_scan_bwd_ws": [_vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _vp, _c_i64,
+                           _vp],
     "fpscan_shard_fwd_reduce": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_fwd_scan": [_vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
     "fpscan_shard_bwd_reduce": [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _vp],
@@ -84,6 +87,7 @@ def load() -> ctypes.CDLL:
             fn.argtypes = argtypes
             fn.restype = {"fpscan_last_error": ctypes.c_char_p,
                           "fpscan_scan_fwd_workspace_bytes": ctypes.c_int64,
+                          "fpscan_scan_bwd_workspace_bytes": ctypes.c_int64,
                           "fpscan_cl_workspace_bytes": ctypes.c_int64,
                           "fpscan_link_bytes": ctypes.c_int64}.get(name, ctypes.c_int)
         ver = lib.fpscan_abi_version()

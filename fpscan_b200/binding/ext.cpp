@@ -8,6 +8,10 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "../../include/fpscan_b200.h"
 
 namespace {
@@ -41,6 +45,22 @@ void check_pair(const at::Tensor& gates, const at::Tensor& tokens, const char* g
   TORCH_CHECK(gates.device() == tokens.device(), gname, " and tokens must be on the same device");
 }
 
+// Workspaces of the split-row paths, one per (device, stream, kind), zeroed
+// once when (re)allocated; calls on one stream are ordered, so they may
+// share it.  Kept for the life of the process (a few KB each).
+at::Tensor workspace(const at::Tensor& like, int64_t bytes, int kind) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, void*, int>, at::Tensor> cache;
+  const auto key = std::make_tuple((int)like.get_device(),
+                                   (void*)at::cuda::getCurrentCUDAStream().stream(), kind);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end() && it->second.numel() >= bytes) return it->second;
+  at::Tensor w = at::zeros({std::max<int64_t>(bytes, 1 << 16)}, like.options().dtype(at::kByte));
+  cache[key] = w;
+  return w;
+}
+
 void raise_on(int rc, const char* what) {
   if (rc != FPSCAN_OK) TORCH_CHECK(false, what, ": ", fpscan_last_error());
 }
@@ -58,10 +78,10 @@ at::Tensor fullscan_forward(const at::Tensor& gates, const at::Tensor& tokens, a
   void* stream = at::cuda::getCurrentCUDAStream().stream();
   const int64_t ws = fpscan_scan_fwd_workspace_bytes(b, d, l, code);
   if (ws > 0) {
-    // few, long rows: the split-row kernel and its (zeroed) workspace
-    at::Tensor w = at::zeros({ws}, tokens.options().dtype(at::kByte));
+    // few, long rows: the split-row kernel and its workspace
+    at::Tensor w = workspace(tokens, ws, 0);
     raise_on(fpscan_scan_fwd_ws(gates.data_ptr(), tokens.data_ptr(), out.data_ptr(), b, d, l, code,
-                                reverse ? 1 : 0, w.data_ptr(), ws, stream),
+                                reverse ? 1 : 0, w.data_ptr(), w.numel(), stream),
              "fpscan_scan_fwd_ws");
   } else {
     raise_on(fpscan_scan_fwd(gates.data_ptr(), tokens.data_ptr(), out.data_ptr(), b, d, l, code,
@@ -83,10 +103,20 @@ std::tuple<at::Tensor, at::Tensor> scan_backward(const at::Tensor& gates, const 
   const int64_t b = grad_out.size(0), d = grad_out.size(1), l = grad_out.size(2);
   const c10::cuda::CUDAGuard guard(grad_out.device());
   at::Tensor dgates = at::empty_like(grad_out), dtokens = at::empty_like(grad_out);
-  raise_on(fpscan_scan_bwd(gates.data_ptr(), y.data_ptr(), grad_out.data_ptr(), dgates.data_ptr(),
-                           dtokens.data_ptr(), b, d, l, code,
-                           at::cuda::getCurrentCUDAStream().stream()),
-           "fpscan_scan_bwd");
+  void* stream = at::cuda::getCurrentCUDAStream().stream();
+  const int64_t ws = fpscan_scan_bwd_workspace_bytes(b, d, l, code);
+  if (ws > 0) {
+    // few, long rows: the split-row backward and its workspace
+    at::Tensor w = workspace(grad_out, ws, 1);
+    raise_on(fpscan_scan_bwd_ws(gates.data_ptr(), y.data_ptr(), grad_out.data_ptr(),
+                                dgates.data_ptr(), dtokens.data_ptr(), b, d, l, code,
+                                w.data_ptr(), w.numel(), stream),
+             "fpscan_scan_bwd_ws");
+  } else {
+    raise_on(fpscan_scan_bwd(gates.data_ptr(), y.data_ptr(), grad_out.data_ptr(),
+                             dgates.data_ptr(), dtokens.data_ptr(), b, d, l, code, stream),
+             "fpscan_scan_bwd");
+  }
   return {dgates, dtokens};
 }
 

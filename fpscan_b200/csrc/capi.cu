@@ -375,6 +375,50 @@ int fpscan_scan_bwd(const void* gates, const void* y, const void* grad_out, void
                        stream);
 }
 
+int64_t fpscan_scan_bwd_workspace_bytes(int64_t batch, int64_t dim, int64_t seqlen, int dtype) {
+  int64_t rows = 0;
+  if (check_dtype(dtype) != FPSCAN_OK) return 0;
+  if (check_shape(batch, dim, seqlen, kRefMinL, kRefMaxL, &rows) != FPSCAN_OK) return 0;
+  const int p = split_bwd_segments(rows, seqlen, dtype, num_sms_current());
+  return split_workspace_bytes(rows, p);
+}
+
+int fpscan_scan_bwd_ws(const void* gates, const void* y, const void* grad_out, void* dgates,
+                       void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
+                       void* workspace, int64_t workspace_bytes, void* stream) {
+  int64_t rows = 0;
+  FPSCAN_TRY(check_dtype(dtype));
+  FPSCAN_TRY(check_shape(batch, dim, seqlen, kRefMinL, kRefMaxL, &rows));
+  if (rows == 0) return ok();
+  const int p = split_bwd_segments(rows, seqlen, dtype, num_sms_current());
+  if (p <= 1)
+    return fpscan_scan_bwd(gates, y, grad_out, dgates, dtokens, batch, dim, seqlen, dtype, stream);
+  FPSCAN_TRY(check_ptr(gates, "gates"));
+  FPSCAN_TRY(check_ptr(y, "y"));
+  FPSCAN_TRY(check_ptr(grad_out, "grad_out"));
+  FPSCAN_TRY(check_ptr(dgates, "dgates"));
+  FPSCAN_TRY(check_ptr(dtokens, "dtokens"));
+  FPSCAN_TRY(check_ptr(workspace, "workspace"));
+  const int64_t need = split_workspace_bytes(rows, p);
+  if (workspace_bytes < need)
+    return fail(FPSCAN_ERR_INVALID, "workspace too small: %lld bytes, need %lld",
+                (long long)workspace_bytes, (long long)need);
+  const uintptr_t bytes = (uintptr_t)(rows * seqlen * dtype_size(dtype));
+  const Span all[6] = {{"gates", (uintptr_t)gates, (uintptr_t)gates + bytes},
+                       {"y", (uintptr_t)y, (uintptr_t)y + bytes},
+                       {"grad_out", (uintptr_t)grad_out, (uintptr_t)grad_out + bytes},
+                       {"workspace", (uintptr_t)workspace, (uintptr_t)workspace + (uintptr_t)need},
+                       {"dgates", (uintptr_t)dgates, (uintptr_t)dgates + bytes},
+                       {"dtokens", (uintptr_t)dtokens, (uintptr_t)dtokens + bytes}};
+  for (int i = 3; i < 6; ++i)
+    for (int j = 0; j < i; ++j)
+      if (overlaps(all[i], all[j]))
+        return fail(FPSCAN_ERR_INVALID, "%s overlaps %s", all[i].name, all[j].name);
+  SplitBwdArgs a{gates,  y,    grad_out, dgates, dtokens, workspace,
+                 rows,   seqlen, p,      dtype,  static_cast<cudaStream_t>(stream)};
+  return cuda_result(launch_split_bwd(a), "fpscan_scan_bwd_ws launch");
+}
+
 int fpscan_scan_bwd_act(const void* z, const void* y, const void* grad_out, void* dz,
                         void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
                         int activation, void* stream) {

@@ -138,6 +138,21 @@ struct SplitArgs {
   cudaStream_t stream;
 };
 
+// Split-row fused backward (scan_split.cu).
+struct SplitBwdArgs {
+  const void* gates;
+  const void* y;
+  const void* grad_out;
+  void* dgates;
+  void* dtokens;
+  void* workspace;      // >= split_workspace_bytes(rows, segments), 16-byte aligned
+  int64_t rows;
+  int64_t seqlen;
+  int64_t segments;     // per row, power of two (split_bwd_segments)
+  int dtype;
+  cudaStream_t stream;
+};
+
 // Scan / backward for any seqlen >= 1 (scan_anylen.cu).
 struct AnyArgs {
   const void* gates;
@@ -207,6 +222,8 @@ int split_slots(int dtype, int num_sms);
 int split_segments(int64_t rows, int64_t seqlen, int dtype, int slots);
 int64_t split_workspace_bytes(int64_t rows, int segments);
 cudaError_t launch_bwd(const BwdArgs& a);
+int split_bwd_segments(int64_t rows, int64_t seqlen, int dtype, int num_sms);
+cudaError_t launch_split_bwd(const SplitBwdArgs& a);
 cudaError_t launch_anylen(const AnyArgs& a);
 cudaError_t launch_cl(const ClArgs& a);
 int64_t cl_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim, int dtype, bool backward);

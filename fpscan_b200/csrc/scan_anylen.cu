@@ -201,6 +201,8 @@ __global__ void __launch_bounds__(kThreads, (AnyCfg<T, NV>::kMinBlocks))
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();  // the previous kernel in the stream is complete from here on
+  pdl_launch_dependents();
 
   int64_t issued = 0;
   auto issue = [&](int64_t k) {
@@ -415,6 +417,8 @@ __global__ void __launch_bounds__(kThreads, (AnyCfg<T, NV>::kBwdMinBlocks))
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();  // the previous kernel in the stream is complete from here on
+  pdl_launch_dependents();
 
   int64_t issued = 0;
   auto issue = [&](int64_t k) {
@@ -629,8 +633,7 @@ static cudaError_t launch_one_wave(Kern kern, int smem, const AnyArgs& a, AnyKPa
   p.rows_per_tile = rpt;
   p.L = a.seqlen;
   p.n_total = a.rows * a.seqlen;
-  kern<<<(unsigned)tiles, kThreads, smem, a.stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(kern, (unsigned)tiles, kThreads, smem, a.stream, p);
 }
 
 template <typename T, int NV>

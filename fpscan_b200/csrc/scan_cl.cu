@@ -134,10 +134,14 @@ __global__ void __launch_bounds__(NTH, 1)
 #pragma unroll
     for (int s = 0; s < S; ++s) mbar_init(&s_bar[s], 1);
     fence_mbar_init();
-    if (!aligned) atomicOr(&g_status, kStatusMisaligned);
   }
   __syncthreads();
-  if (!aligned) return;
+  pdl_wait();  // the previous kernel in the stream is complete from here on
+  pdl_launch_dependents();
+  if (!aligned) {
+    if (tid == 0) atomicOr(&g_status, kStatusMisaligned);
+    return;
+  }
 
   const int x = (int)(cblk * kStreamVecs * V);
   int64_t issued = 0;  // local chunk index
@@ -324,8 +328,18 @@ __global__ void __launch_bounds__(NTH, 1)
 // Entering state of every segment after the first, per (column, vector,
 // channel): the first segment's map holds its last state (it starts at the
 // head); later ones compose A * state + B.
-__global__ void cl_seg_carry_kernel(const float2* __restrict__ seg_map, float* __restrict__ seg_carry,
-                                    int64_t chans, int64_t ncol, int64_t nseg) {
+struct CarryArgs {
+  const float2* seg_map;
+  float* seg_carry;
+  int64_t chans, ncol, nseg;
+};
+
+__global__ void cl_seg_carry_kernel(const CarryArgs ca) {
+  const float2* __restrict__ seg_map = ca.seg_map;
+  float* __restrict__ seg_carry = ca.seg_carry;
+  const int64_t chans = ca.chans, ncol = ca.ncol, nseg = ca.nseg;
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= ncol * chans) return;
   const int64_t col = i / chans, ch = i - col * chans;
@@ -470,8 +484,7 @@ cudaError_t launch_stream_t(const ClArgs& a) {
   if (plan.nseg == 1) {
     auto kern = scan_cl_stream_kernel<T, MODE, TW, S, NTH, 0>;
     if ((e = configure(kern, smem, conf0)) != cudaSuccess) return e;
-    kern<<<(unsigned)cols, NTH, smem, a.stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(kern, (unsigned)cols, NTH, smem, a.stream, p);
   }
   // segmented: reduce, compose, scan
   const int64_t chans = (int64_t)kStreamVecs * V;
@@ -485,12 +498,13 @@ cudaError_t launch_stream_t(const ClArgs& a) {
   auto k2 = scan_cl_stream_kernel<T, MODE, TW, S, NTH, 2>;
   if ((e = configure(k1, smem, conf1)) != cudaSuccess) return e;
   if ((e = configure(k2, smem, conf2)) != cudaSuccess) return e;
-  k1<<<grid, NTH, smem, a.stream>>>(p);
+  if ((e = launch_pdl(k1, grid, NTH, smem, a.stream, p)) != cudaSuccess) return e;
   const int64_t threads = cols * chans;
-  cl_seg_carry_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, a.stream>>>(
-      p.seg_map, const_cast<float*>(p.seg_carry), chans, cols, plan.nseg);
-  k2<<<grid, NTH, smem, a.stream>>>(p);
-  return cudaGetLastError();
+  CarryArgs ca{p.seg_map, const_cast<float*>(p.seg_carry), chans, cols, plan.nseg};
+  if ((e = launch_pdl(cl_seg_carry_kernel, (unsigned)((threads + 255) / 256), 256, 0, a.stream,
+                      ca)) != cudaSuccess)
+    return e;
+  return launch_pdl(k2, grid, NTH, smem, a.stream, p);
 }
 
 // Streaming-kernel shape: TW timesteps per thread group, S ring stages and

@@ -55,7 +55,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .ops import DTYPE_CODES, pscan, scan_backward, scan_forward, validate
+from .ops import DTYPE_CODES, nvtx_range, pscan, scan_backward, scan_forward, validate
 
 import ctypes
 
@@ -177,13 +177,16 @@ class SeqShardedPScan(torch.autograd.Function):
     def forward(ctx, gates, tokens, group, ops):
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
-        carry = ops.fwd_reduce(gates, tokens)                    # [2, rows]: (A_r, B_r)
-        gathered = _all_gather_maps(carry, world, group)         # [world, 2, rows]
-        y_init = ops.combine(gathered, world, rank, reverse=False)
-        if rank == 0:
-            y = ops.fwd_scan_zero(gates, tokens)
-        else:
-            y = ops.fwd_scan(gates, tokens, y_init)
+        with nvtx_range("fpscan.seq.forward.reduce"):
+            carry = ops.fwd_reduce(gates, tokens)                # [2, rows]: (A_r, B_r)
+        with nvtx_range("fpscan.seq.forward.exchange"):
+            gathered = _all_gather_maps(carry, world, group)     # [world, 2, rows]
+            y_init = ops.combine(gathered, world, rank, reverse=False)
+        with nvtx_range("fpscan.seq.forward.scan"):
+            if rank == 0:
+                y = ops.fwd_scan_zero(gates, tokens)
+            else:
+                y = ops.fwd_scan(gates, tokens, y_init)
         ctx.save_for_backward(gates, y, carry[0].clone(), y_init)
         ctx.group, ctx.ops, ctx.world, ctx.rank = group, ops, world, rank
         return y
@@ -193,13 +196,16 @@ class SeqShardedPScan(torch.autograd.Function):
         gates, y, a_local, y_init = ctx.saved_tensors
         ops, world, rank = ctx.ops, ctx.world, ctx.rank
         grad_out = grad_out.contiguous()
-        v = ops.bwd_reduce(gates, grad_out)
-        gathered = _all_gather_maps(torch.stack([a_local, v]), world, ctx.group)
-        addend = ops.combine(gathered, world, rank, reverse=True)
-        if world == 1:
-            dg, dt = ops.bwd_scan_zero(gates, y, grad_out)
-        else:
-            dg, dt = ops.bwd_scan(gates, y, grad_out, addend, y_init)
+        with nvtx_range("fpscan.seq.backward.reduce"):
+            v = ops.bwd_reduce(gates, grad_out)
+        with nvtx_range("fpscan.seq.backward.exchange"):
+            gathered = _all_gather_maps(torch.stack([a_local, v]), world, ctx.group)
+            addend = ops.combine(gathered, world, rank, reverse=True)
+        with nvtx_range("fpscan.seq.backward.scan"):
+            if world == 1:
+                dg, dt = ops.bwd_scan_zero(gates, y, grad_out)
+            else:
+                dg, dt = ops.bwd_scan(gates, y, grad_out, addend, y_init)
         return dg, dt, None, None
 
 
@@ -349,7 +355,7 @@ class ChainedSeqShardedPScan(torch.autograd.Function):
                   if chain.prev else None)
         chain.check(block=False)
         e = chain.next_fwd_epoch()
-        with torch.cuda.device(tokens.device):
+        with torch.cuda.device(tokens.device), nvtx_range("fpscan.chain.forward"):
             _lib.call("fpscan_shard_fwd_link", gates.data_ptr(), tokens.data_ptr(), y.data_ptr(),
                       y_init.data_ptr() if y_init is not None else None, rows, L, code,
                       chain.local, chain.prev, chain.next, e, chain.depth,
@@ -369,7 +375,7 @@ class ChainedSeqShardedPScan(torch.autograd.Function):
         dt = torch.empty_like(grad_out)
         chain.check(block=False)
         e = chain.next_bwd_epoch()
-        with torch.cuda.device(grad_out.device):
+        with torch.cuda.device(grad_out.device), nvtx_range("fpscan.chain.backward"):
             _lib.call("fpscan_shard_bwd_link", gates.data_ptr(), y.data_ptr(), grad_out.data_ptr(),
                       dg.data_ptr(), dt.data_ptr(), y_init.data_ptr() if ctx.has_init else None,
                       rows, L, DTYPE_CODES[grad_out.dtype], chain.local, chain.prev, chain.next,

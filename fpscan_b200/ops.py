@@ -16,6 +16,7 @@ path.
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -27,6 +28,31 @@ __all__ = ["pscan", "scan_forward", "PScan", "pscan_gated", "scan_forward_gated"
            "scan_forward_channels_last"]
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+# NVTX ranges around the forward and backward (for nsys / ncu timelines):
+# FPSCAN_B200_NVTX=1 turns them on; off, the ops pay nothing for them.
+NVTX = os.environ.get("FPSCAN_B200_NVTX", "0") == "1"
+
+
+class _Range:
+    __slots__ = ("name",)
+
+    def __init__(self, name: str):
+        self.name = name
+
+    def __enter__(self):
+        if NVTX:
+            torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *exc):
+        if NVTX:
+            torch.cuda.nvtx.range_pop()
+        return False
+
+
+def nvtx_range(name: str) -> _Range:
+    """Context manager: an NVTX range named `name` when FPSCAN_B200_NVTX=1."""
+    return _Range(name)
 MIN_SEQLEN = 32
 MAX_SEQLEN = 65536
 
@@ -242,9 +268,24 @@ def scan_backward(gates: torch.Tensor, y: torch.Tensor, grad_output: torch.Tenso
     dgates = torch.empty_like(grad_output)
     dtokens = torch.empty_like(grad_output)
     b, d, l = grad_output.shape
-    _launch(grad_output.get_device(), "fpscan_scan_bwd", gates.data_ptr(), y.data_ptr(),
-            grad_output.data_ptr(), dgates.data_ptr(), dtokens.data_ptr(), b, d, l,
-            DTYPE_CODES[grad_output.dtype])
+    code = DTYPE_CODES[grad_output.dtype]
+    dev = grad_output.get_device()
+    key = (b * d, l, code, dev, "bwd")
+    ws_bytes = _ws_need.get(key)
+    if ws_bytes is None:
+        prev = _get_device()
+        torch.cuda.set_device(dev)
+        try:
+            ws_bytes = _ws_need[key] = _lib.load().fpscan_scan_bwd_workspace_bytes(b, d, l, code)
+        finally:
+            torch.cuda.set_device(prev)
+    if ws_bytes > 0:  # few, long rows: the split-row backward
+        ws = _workspace(grad_output.device, _raw_stream(dev), ws_bytes, kind="split_bwd")
+        _launch(dev, "fpscan_scan_bwd_ws", gates.data_ptr(), y.data_ptr(), grad_output.data_ptr(),
+                dgates.data_ptr(), dtokens.data_ptr(), b, d, l, code, ws.data_ptr(), ws.numel())
+    else:
+        _launch(dev, "fpscan_scan_bwd", gates.data_ptr(), y.data_ptr(), grad_output.data_ptr(),
+                dgates.data_ptr(), dtokens.data_ptr(), b, d, l, code)
     return dgates, dtokens
 
 
@@ -254,7 +295,11 @@ class PScan(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, gates: torch.Tensor, tokens: torch.Tensor) -> torch.Tensor:
-        out = scan_forward(gates, tokens)
+        if NVTX:
+            with nvtx_range("fpscan.forward"):
+                out = scan_forward(gates, tokens)
+        else:
+            out = scan_forward(gates, tokens)
         ctx.save_for_backward(gates, out)
         return out
 
@@ -262,6 +307,9 @@ class PScan(torch.autograd.Function):
     def backward(ctx, grad_output: torch.Tensor):
         gates, out = ctx.saved_tensors
         grad_output = grad_output.contiguous()
+        if NVTX:
+            with nvtx_range("fpscan.backward"):
+                return scan_backward(gates, out, grad_output)
         return scan_backward(gates, out, grad_output)
 
 

@@ -208,6 +208,26 @@ FPSCAN_API int fpscan_scan_bwd(const void* gates, const void* y, const void* gra
                     void* dtokens, int64_t batch, int64_t dim, int64_t seqlen, int dtype,
                     void* stream);
 
+/*
+ * fpscan_scan_bwd for few, long rows: rows are cut into segments processed
+ * by separate CTAs with a decoupled look-back on the dtokens state (the
+ * split-row scheme of fpscan_scan_fwd_ws, run from each row's end).
+ * `workspace` (16-byte aligned; zero it once after allocating it, as for
+ * fpscan_scan_fwd_ws) of at least fpscan_scan_bwd_workspace_bytes(...)
+ * bytes; that query returns 0 for
+ * shapes the split-row path does not take, and then this call is
+ * fpscan_scan_bwd.  Outputs must not overlap any input, each other or the
+ * workspace.  Calls sharing one workspace must be ordered (one stream).
+ * Extends fpscan_scan_bwd, which replaces the composition in
+ * PScan.backward (reference fpscan/ops.py:70-83).
+ */
+FPSCAN_API int64_t fpscan_scan_bwd_workspace_bytes(int64_t batch, int64_t dim, int64_t seqlen,
+                                                   int dtype);
+FPSCAN_API int fpscan_scan_bwd_ws(const void* gates, const void* y, const void* grad_out,
+                                  void* dgates, void* dtokens, int64_t batch, int64_t dim,
+                                  int64_t seqlen, int dtype, void* workspace,
+                                  int64_t workspace_bytes, void* stream);
+
 /* ---- Sequence-sharded building blocks (no reference counterpart: the
  * reference has no multi-GPU path).  A shard holds `rows` rows of `seqlen`
  * (power of two, >= 32, <= 2^24) consecutive positions of longer sequences. */

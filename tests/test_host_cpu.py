@@ -267,3 +267,13 @@ def test_row_unit_claim_protocol(tmp_path):
                     os.path.join(here, "claim_protocol_check.cpp"), "-o", str(exe)], check=True)
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-3000:]
+
+
+def test_nvtx_ranges_are_opt_in():
+    """NVTX ranges wrap the forward, backward and sequence-shard steps only
+    when FPSCAN_B200_NVTX=1; the range object is a no-op otherwise."""
+    from fpscan_b200 import ops as o
+
+    assert o.NVTX is False or os.environ.get("FPSCAN_B200_NVTX") == "1"
+    with o.nvtx_range("fpscan.test"):
+        pass

@@ -672,3 +672,69 @@ def test_ws_path_guarded(dtype, batch, dim, seqlen):
             _check(g.out, ref, dtype, f"fwd_ws rev={rev}")
     torch.cuda.synchronize()
     assert _lib.device_status(clear=True) == 0
+
+
+# ----------------------------------------------------------------- split-row fused backward
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("batch,dim,seqlen", [(2, 4, 65536), (1, 1, 65536), (1, 64, 65536),
+                                              (2, 3, 32768), (1, 5, 32768)])
+def test_split_row_backward(dtype, batch, dim, seqlen):
+    """fpscan_scan_bwd_ws (rows cut into segments processed from each row's
+    end, decoupled look-back on the dtokens state) against fpscan_scan_bwd
+    and float64, outputs guard-banded, three calls in a row on one
+    workspace."""
+    from guard import guarded
+
+    lib = _lib.load()
+    code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[dtype]
+    gates, tokens = _make_inputs(batch, dim, seqlen, dtype, seed=seqlen + dim + 7)
+    gen = torch.Generator(device=DEVICE).manual_seed(dim)
+    go = torch.randn(batch, dim, seqlen, generator=gen, device=DEVICE).to(dtype)
+    y = fpscan.scan_forward(gates, tokens)
+    need = lib.fpscan_scan_bwd_workspace_bytes(batch, dim, seqlen, code)
+    assert need > 0  # these shapes take the split-row path
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEVICE)
+    s = torch.cuda.current_stream().cuda_stream
+    dg_p, dt_p = torch.empty_like(go), torch.empty_like(go)
+    _lib.check(lib.fpscan_scan_bwd(gates.data_ptr(), y.data_ptr(), go.data_ptr(), dg_p.data_ptr(),
+                                   dt_p.data_ptr(), batch, dim, seqlen, code, s), "bwd")
+    y64 = oracle.scan_f64(_np64(gates), _np64(tokens))
+    dg64, dt64 = oracle.scan_bwd_f64(_np64(gates), _np64(y), _np64(go))
+    for _ in range(3):
+        dg, dt = guarded(go.shape, dtype), guarded(go.shape, dtype)
+        _lib.check(lib.fpscan_scan_bwd_ws(gates.data_ptr(), y.data_ptr(), go.data_ptr(),
+                                          dg.out.data_ptr(), dt.out.data_ptr(), batch, dim,
+                                          seqlen, code, ws.data_ptr(), ws.numel(), s), "bwd_ws")
+        dg.check("split bwd dgates")
+        dt.check("split bwd dtokens")
+        _assert_normwise(dt.out, dt64, dtype, "split dtokens")
+        _assert_normwise(dg.out, dg64, dtype, "split dgates")
+        assert oracle.normwise_error(_np64(dt.out), _np64(dt_p)) <= NORM_TOL[dtype]
+        assert oracle.normwise_error(_np64(dg.out), _np64(dg_p)) <= NORM_TOL[dtype]
+    # the public API takes the same path
+    gr, xr = gates.clone().requires_grad_(), tokens.clone().requires_grad_()
+    dgr, dxr = torch.autograd.grad(fpscan.pscan(gr, xr), (gr, xr), go)
+    _assert_normwise(dxr, dt64, dtype, "pscan dtokens")
+    _assert_normwise(dgr, dg64, dtype, "pscan dgates")
+    torch.cuda.synchronize()
+    assert _lib.device_status(clear=True) == 0
+    del y64
+
+
+def test_split_row_backward_workspace_checks():
+    lib = _lib.load()
+    assert lib.fpscan_scan_bwd_workspace_bytes(64, 1024, 4096, 0) == 0  # many rows: none
+    gates, tokens = _make_inputs(1, 2, 65536, torch.float32)
+    need = lib.fpscan_scan_bwd_workspace_bytes(1, 2, 65536, 0)
+    assert need > 0
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEVICE)
+    dg, dt = torch.empty_like(tokens), torch.empty_like(tokens)
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.fpscan_scan_bwd_ws(gates.data_ptr(), tokens.data_ptr(), tokens.data_ptr(),
+                                  dg.data_ptr(), dt.data_ptr(), 1, 2, 65536, 0, ws.data_ptr(),
+                                  need - 16, s) == 1
+    assert b"workspace" in lib.fpscan_last_error()
+    assert lib.fpscan_scan_bwd_ws(gates.data_ptr(), tokens.data_ptr(), tokens.data_ptr(),
+                                  dg.data_ptr(), dg.data_ptr(), 1, 2, 65536, 0, ws.data_ptr(),
+                                  need, s) == 1
+    assert b"overlaps" in lib.fpscan_last_error()
