@@ -57,6 +57,7 @@ SIGNATURES = {
     "fpscan_device_status": [ctypes.POINTER(ctypes.c_uint), _c_int],
     "fpscan_status_snapshot": [_vp, _vp],
     "fpscan_set_wait_limit_ns": [ctypes.c_uint64],
+    "fpscan_debug_bounds": [_vp],
 }
 
 EXPECTED_ABI_VERSION = 1
@@ -67,6 +68,24 @@ _lib = None
 
 class FpscanError(RuntimeError):
     """A C-ABI call returned a non-zero status."""
+
+
+_RESTYPES = {"fpscan_last_error": ctypes.c_char_p,
+             "fpscan_scan_fwd_workspace_bytes": ctypes.c_int64,
+             "fpscan_scan_bwd_workspace_bytes": ctypes.c_int64,
+             "fpscan_cl_workspace_bytes": ctypes.c_int64,
+             "fpscan_link_bytes": ctypes.c_int64}
+
+
+def open_library(path: str) -> ctypes.CDLL:
+    """Load a build of the C ABI at `path` (e.g. the bounds-checking
+    libfpscan_b200_debug.so) with the signatures set up; not cached."""
+    lib = ctypes.CDLL(path)
+    for name, argtypes in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = _RESTYPES.get(name, ctypes.c_int)
+    return lib
 
 
 def load() -> ctypes.CDLL:
@@ -81,15 +100,7 @@ def load() -> ctypes.CDLL:
             raise ImportError(
                 f"fpscan_b200 CUDA library not found at {LIB_PATH}; build it with "
                 "`python -m fpscan_b200.build` (needs nvcc for sm_100a)")
-        lib = ctypes.CDLL(LIB_PATH)
-        for name, argtypes in SIGNATURES.items():
-            fn = getattr(lib, name)
-            fn.argtypes = argtypes
-            fn.restype = {"fpscan_last_error": ctypes.c_char_p,
-                          "fpscan_scan_fwd_workspace_bytes": ctypes.c_int64,
-                          "fpscan_scan_bwd_workspace_bytes": ctypes.c_int64,
-                          "fpscan_cl_workspace_bytes": ctypes.c_int64,
-                          "fpscan_link_bytes": ctypes.c_int64}.get(name, ctypes.c_int)
+        lib = open_library(LIB_PATH)
         ver = lib.fpscan_abi_version()
         if ver != EXPECTED_ABI_VERSION:
             raise ImportError(f"libfpscan_b200 ABI version {ver}, expected {EXPECTED_ABI_VERSION}")
@@ -120,6 +131,7 @@ STATUS_BITS = {
     2: "a split-row scan gave up waiting for a preceding segment (look-back)",
     4: "a channel-last CTA found its staging buffer misaligned and skipped its work",
     8: "a chained sequence-sharded scan gave up waiting for a neighbouring rank",
+    16: "a kernel skipped a global access outside its tensor (bounds-checking build)",
 }
 
 

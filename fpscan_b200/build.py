@@ -94,6 +94,23 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     return out_path
 
 
+# ---------------------------------------------------------------- bounds-checking build
+DEBUG_LIB_PATH = os.path.join(PKG_DIR, "libfpscan_b200_debug.so")
+
+
+def build_debug(force: bool = False, verbose: bool = False) -> str:
+    """Compile libfpscan_b200_debug.so: the same library with
+    -DFPSCAN_DEBUG_BOUNDS, whose kernels check every global access they
+    compute themselves against its tensor's extent and record (and skip) one
+    outside it in the device status word.  A test tool: the stand-in for the
+    memory checkers that are closed on the GPU pool."""
+    if (not force and os.path.exists(DEBUG_LIB_PATH)
+            and all(os.path.getmtime(p) <= os.path.getmtime(DEBUG_LIB_PATH) for p in _deps())):
+        return DEBUG_LIB_PATH
+    return build(force=True, verbose=verbose, defines=("FPSCAN_DEBUG_BOUNDS",),
+                 out_path=DEBUG_LIB_PATH)
+
+
 # ---------------------------------------------------------------- torch binding
 BINDING_SRC = os.path.join(PKG_DIR, "binding", "ext.cpp")
 BINDING_PATH = os.path.join(PKG_DIR, "_ext.so")

@@ -23,6 +23,13 @@ __device__ unsigned long long g_wait_limit_ns = 2000000000ull;
 namespace {
 // Reads and clears the status word into *dst (device or mapped host memory).
 __global__ void status_take_kernel(unsigned* dst) { *dst = atomicExch(&g_status, 0u); }
+
+// Bounds-checking builds: checks (without accessing it) an address one
+// element past a 4-element extent, which records kStatusBounds.  Release
+// builds: an empty kernel.
+__global__ void bounds_probe_kernel() {
+  FPSCAN_DEBUG_ONLY(__shared__ float extent[4]; in_bounds<4>(extent + 4, 4, extent, extent + 4);)
+}
 }  // namespace
 
 namespace {
@@ -532,6 +539,16 @@ int fpscan_carry_combine(const float* gathered, int world, int rank, int64_t row
   return cuda_result(launch_carry_combine(gathered, world, rank, rows, reverse ? 1 : 0, out,
                                           static_cast<cudaStream_t>(stream)),
                      "fpscan_carry_combine launch");
+}
+
+int fpscan_debug_bounds(void* stream) {
+  bounds_probe_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>();
+  if (cudaGetLastError() != cudaSuccess) return -1;
+#ifdef FPSCAN_DEBUG_BOUNDS
+  return 1;
+#else
+  return 0;
+#endif
 }
 
 int fpscan_set_wait_limit_ns(uint64_t ns) {

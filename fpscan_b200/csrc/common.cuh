@@ -30,6 +30,7 @@ enum : unsigned {
   kStatusLookbackTimeout = 2u,
   kStatusMisaligned = 4u,
   kStatusLinkTimeout = 8u,
+  kStatusBounds = 16u,
 };
 
 extern __device__ unsigned int g_status;
@@ -99,6 +100,31 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
           smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
+}
+
+// Debug builds (-DFPSCAN_DEBUG_BOUNDS: libfpscan_b200_debug.so, built by
+// fpscan_b200.build.build_debug) check every global access that a kernel
+// computes itself -- bulk-copy sources, direct loads, output stores, carry
+// arrays -- against the extent [lo, hi) of the tensor it belongs to and the
+// access's alignment; an access outside is skipped and recorded as
+// kStatusBounds, so a wrong index shows up as a status bit instead of a
+// fault or a silent write elsewhere.  The checks sit inside
+// FPSCAN_DEBUG_ONLY(...), which release builds drop, so the release kernels
+// are compiled from unchanged code (same registers, same schedule).
+#ifdef FPSCAN_DEBUG_BOUNDS
+#define FPSCAN_DEBUG_ONLY(...) __VA_ARGS__
+#else
+#define FPSCAN_DEBUG_ONLY(...)
+#endif
+
+template <int ALIGN = 16>
+__device__ __forceinline__ bool in_bounds(const void* p, uint64_t bytes, const void* lo,
+                                          const void* hi) {
+  const char* c = static_cast<const char*>(p);
+  const bool ok = c >= static_cast<const char*>(lo) && c + bytes <= static_cast<const char*>(hi) &&
+                  (reinterpret_cast<uintptr_t>(c) % ALIGN) == 0;
+  if (!ok) atomicOr(&g_status, kStatusBounds);
+  return ok;
 }
 
 // Programmatic dependent launch.  A kernel launched with the programmatic

@@ -123,18 +123,21 @@ __device__ __forceinline__ void block_seg_prefix(const float4* wt, int lane, int
 // element e0, only for elements inside [ts, te).
 template <typename T, int NV>
 __device__ __forceinline__ void store_masked(T* dst, int64_t e0, int64_t ts, int64_t te,
-                                             const float* f) {
+                                             const float* f FPSCAN_DEBUG_ONLY(, int64_t n)) {
   constexpr int V = Elem<T>::kVec;
 #pragma unroll
   for (int q = 0; q < NV; ++q) {
     const int64_t vs = e0 + q * V;
     if (vs >= ts && vs + V <= te) {
+      FPSCAN_DEBUG_ONLY(if (in_bounds(dst + vs, 16, dst, dst + n)))
       reinterpret_cast<uint4*>(dst + vs)[0] = pack_vec<T>(f + q * V);
     } else {
 #pragma unroll
       for (int j = 0; j < V; ++j) {
         const int64_t t = vs + j;
-        if (t >= ts && t < te) dst[t] = Elem<T>::store(f[q * V + j]);
+        if (t >= ts && t < te FPSCAN_DEBUG_ONLY(
+                                  && in_bounds<sizeof(T)>(dst + t, sizeof(T), dst, dst + n)))
+          dst[t] = Elem<T>::store(f[q * V + j]);
       }
     }
   }
@@ -211,6 +214,13 @@ __global__ void __launch_bounds__(kThreads, (AnyCfg<T, NV>::kMinBlocks))
     const int64_t ce = min(min(cs + CH, te_up), n_floor);
     const uint32_t bytes = ce > cs ? (uint32_t)((ce - cs) * (int64_t)sizeof(T)) : 0u;
     const int s = (int)(k % S);
+    // debug builds: a copy outside its tensor is skipped, the stage completes
+    FPSCAN_DEBUG_ONLY(
+        if (bytes && (!in_bounds(gates + cs, bytes, gates, gates + N) ||
+                      !in_bounds(tokens + cs, bytes, tokens, tokens + N))) {
+          mbar_expect_tx(&s_bar[s], 0u);
+          return;
+        })
     mbar_expect_tx(&s_bar[s], 2u * bytes);
     if (bytes) {
       bulk_g2s(s_g[s], gates + cs, bytes, &s_bar[s]);
@@ -348,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, (AnyCfg<T, NV>::kMinBlocks))
         for (int i = 0; i < E; ++i)
           f[REV ? E - 1 - i : i] = ((incl >> i) & 1u) ? b[i] : fmaf(a[i], state, b[i]);
       }
-      store_masked<T, NV>(out, e0, ts, te, f);
+      store_masked<T, NV>(out, e0, ts, te, f FPSCAN_DEBUG_ONLY(, N));
     }
 
     carry = cf ? cb : fmaf(ca, carry, cb);
@@ -435,6 +445,14 @@ __global__ void __launch_bounds__(kThreads, (AnyCfg<T, NV>::kBwdMinBlocks))
     const uint32_t g_bytes = (uint32_t)((ge - cs) * (int64_t)sizeof(T));
     const bool y_halo = cs > as;
     const uint32_t y_bytes = bytes + (y_halo ? 16u : 0u);
+    // debug builds: a copy outside its tensor is skipped, the stage completes
+    FPSCAN_DEBUG_ONLY(
+        if (!in_bounds(gates + cs, g_bytes, gates, gates + N) ||
+            !in_bounds(gout + cs, bytes, gout, gout + N) ||
+            !in_bounds(y_halo ? y + cs - V : y + cs, y_bytes, y, y + N)) {
+          mbar_expect_tx(&s_bar[s], 0u);
+          return;
+        })
     mbar_expect_tx(&s_bar[s], g_bytes + bytes + y_bytes);
     bulk_g2s(s_g + s * GS, gates + cs, g_bytes, &s_bar[s]);
     bulk_g2s(s_go + s * SV, gout + cs, bytes, &s_bar[s]);
@@ -591,8 +609,8 @@ __global__ void __launch_bounds__(kThreads, (AnyCfg<T, NV>::kBwdMinBlocks))
           f_dg[j] = dt * yp;
         }
       }
-      store_masked<T, NV>(dtok, e0, ts, te, f_dt);
-      store_masked<T, NV>(dgates, e0, ts, te, f_dg);
+      store_masked<T, NV>(dtok, e0, ts, te, f_dt FPSCAN_DEBUG_ONLY(, N));
+      store_masked<T, NV>(dgates, e0, ts, te, f_dg FPSCAN_DEBUG_ONLY(, N));
     }
 
     carry = cf ? cb : fmaf(ca, carry, cb);

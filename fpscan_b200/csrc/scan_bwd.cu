@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lg = p.lg;
   const int64_t Lmask = (int64_t(1) << lg) - 1;
+  FPSCAN_DEBUG_ONLY(const int64_t n_el = p.rows << lg;)  // elements of each tensor
   if ((int64_t)blockIdx.x >= p.us.nunits) return;
   // Units and chunk hand-over as in scan_fwd.cu; link variants (always
   // statically tiled) compute their chunk positions in every thread.
@@ -143,14 +144,23 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
     if (HAS_OUT) y_bytes = bytes + (off > 0 ? 16u : 0u);
     s_abs[s] = abs;
     s_cnt[s] = cnt;
-    mbar_expect_tx(&s_bar[s], g_bytes + bytes + y_bytes);
-    bulk_g2s(s_g + s * GS, gates + abs, g_bytes, &s_bar[s]);
-    bulk_g2s(s_go + s * SV, gout + abs, bytes, &s_bar[s]);
-    if (HAS_OUT) {
-      if (off > 0)
-        bulk_g2s(s_y + s * YS, y + abs - V, y_bytes, &s_bar[s]);
-      else
-        bulk_g2s(s_y + s * YS + 1, y + abs, y_bytes, &s_bar[s]);
+    // debug builds: a copy outside its tensor is skipped, the stage completes
+    FPSCAN_DEBUG_ONLY(
+        if (!in_bounds(gates + abs, g_bytes, gates, gates + n_el) ||
+            !in_bounds(gout + abs, bytes, gout, gout + n_el) ||
+            (HAS_OUT && !in_bounds(off > 0 ? y + abs - V : y + abs, y_bytes, y, y + n_el))) {
+          mbar_arrive(&s_bar[s]);
+        } else)
+    {
+      mbar_expect_tx(&s_bar[s], g_bytes + bytes + y_bytes);
+      bulk_g2s(s_g + s * GS, gates + abs, g_bytes, &s_bar[s]);
+      bulk_g2s(s_go + s * SV, gout + abs, bytes, &s_bar[s]);
+      if (HAS_OUT) {
+        if (off > 0)
+          bulk_g2s(s_y + s * YS, y + abs - V, y_bytes, &s_bar[s]);
+        else
+          bulk_g2s(s_y + s * YS + 1, y + abs, y_bytes, &s_bar[s]);
+      }
     }
     if (++ps.k == ps.nck) {
       ps.k = 0;
@@ -316,6 +326,8 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
       if constexpr (HAS_OUT) {
         uint4* d1 = reinterpret_cast<uint4*>(dtok + abs) + vi * NV;
         uint4* d2 = reinterpret_cast<uint4*>(dgates + abs) + vi * NV;
+        FPSCAN_DEBUG_ONLY(if (in_bounds(d1, NV * 16, dtok, dtok + n_el) &&
+                              in_bounds(d2, NV * 16, dgates, dgates + n_el)))
 #pragma unroll
         for (int q = 0; q < NV; ++q) {
           d1[q] = pack_vec<T>(f_dt + q * V);
@@ -329,7 +341,8 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
             st_relaxed_sys_u64(p.lk.out_word + row, link_word(v, p.lk.epoch));
           }
         }
-      } else if (grp_row_first) {
+      } else if (grp_row_first FPSCAN_DEBUG_ONLY(
+                     && in_bounds<4>(p.carry_b + row, 4, p.carry_b, p.carry_b + p.rows))) {
         p.carry_b[row] = gcur * d;  // plain scan only
       }
     }

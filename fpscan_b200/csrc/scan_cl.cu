@@ -85,6 +85,8 @@ struct StreamParams {
   int64_t cb;    // column blocks per batch (ceil(dv / 8))
   int64_t nseg;  // time segments per column (1: the whole column per CTA)
   int64_t cps;   // chunks per segment
+  int64_t n_el;  // elements of each tensor (bounds checks of debug builds)
+  int64_t n_map; // seg_map entries (bounds checks of debug builds)
   float2* seg_map;          // SPLIT 1: per (column, segment, vector, channel) map (A, B)
   const float* seg_carry;   // SPLIT 2: state entering each segment (same indexing)
 };
@@ -293,12 +295,14 @@ __global__ void __launch_bounds__(NTH, 1)
 #pragma unroll
       for (int c = 0; c < V; ++c) st[c] = head ? xx[c] : fmaf(g[c], st[c], xx[c]);
       if (SPLIT != 1 && t >= 0 && t < L && lane_ok) {
+        FPSCAN_DEBUG_ONLY(if (in_bounds(out + base + t * row_elems, 16, out, out + p.n_el)))
         *reinterpret_cast<uint4*>(out + base + t * row_elems) = pack_vec<T>(st);
         if (BWD) {
           float yp[V], dg[V];
           unpack<T>(s_c[lr * kStreamVecs + vec], yp);
 #pragma unroll
           for (int c = 0; c < V; ++c) dg[c] = st[c] * yp[c];
+          FPSCAN_DEBUG_ONLY(if (in_bounds(out2 + base + t * row_elems, 16, out2, out2 + p.n_el)))
           *reinterpret_cast<uint4*>(out2 + base + t * row_elems) = pack_vec<T>(dg);
         }
       }
@@ -320,6 +324,7 @@ __global__ void __launch_bounds__(NTH, 1)
   }
   if (SPLIT == 1 && !aborted && tg == Cfg::NG - 1 && lane_ok) {
     float2* o = p.seg_map + ((col * p.nseg + seg) * kStreamVecs + vec) * V;
+    FPSCAN_DEBUG_ONLY(if (in_bounds<8>(o, V * 8, p.seg_map, p.seg_map + p.n_map)))
 #pragma unroll
     for (int c = 0; c < V; ++c) o[c] = make_float2(seg_a[c], st[c]);
   }
@@ -481,6 +486,7 @@ cudaError_t launch_stream_t(const ClArgs& a) {
   const SegPlan plan = cl_seg_plan(cols, a.seqlen, R);
   p.nseg = plan.nseg;
   p.cps = plan.cps;
+  p.n_el = a.batch * a.seqlen * a.dim;
   if (plan.nseg == 1) {
     auto kern = scan_cl_stream_kernel<T, MODE, TW, S, NTH, 0>;
     if ((e = configure(kern, smem, conf0)) != cudaSuccess) return e;
@@ -492,6 +498,7 @@ cudaError_t launch_stream_t(const ClArgs& a) {
   const int64_t map_bytes = (n * 8 + 255) / 256 * 256;
   if ((int64_t)a.workspace_bytes < map_bytes + n * 4) return cudaErrorInvalidValue;
   p.seg_map = static_cast<float2*>(a.workspace);
+  p.n_map = n;
   p.seg_carry = reinterpret_cast<const float*>(static_cast<char*>(a.workspace) + map_bytes);
   const unsigned grid = (unsigned)(cols * plan.nseg);
   auto k1 = scan_cl_stream_kernel<T, MODE, TW, S, NTH, 1>;

@@ -98,6 +98,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int lg = p.lg;
   const int64_t Lmask = (int64_t(1) << lg) - 1;
+  FPSCAN_DEBUG_ONLY(const int64_t n_el = p.rows << lg;)  // elements of each tensor
   if ((int64_t)blockIdx.x >= p.us.nunits) return;
   // Units are flat streams of whole rows (chunks never straddle units, and a
   // unit starts a row, so an element's position in its row is abs & Lmask).
@@ -151,9 +152,17 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     const uint32_t bytes = (uint32_t)cnt * (uint32_t)sizeof(T);
     s_abs[s] = abs;
     s_cnt[s] = cnt;
-    mbar_expect_tx(&s_bar[s], 2u * bytes);
-    bulk_g2s(s_g[s], gates + abs, bytes, &s_bar[s]);
-    bulk_g2s(s_x[s], tokens + abs, bytes, &s_bar[s]);
+    // debug builds: a copy outside its tensor is skipped, the stage completes
+    FPSCAN_DEBUG_ONLY(
+        if (!in_bounds(gates + abs, bytes, gates, gates + n_el) ||
+            !in_bounds(tokens + abs, bytes, tokens, tokens + n_el)) {
+          mbar_arrive(&s_bar[s]);
+        } else)
+    {
+      mbar_expect_tx(&s_bar[s], 2u * bytes);
+      bulk_g2s(s_g[s], gates + abs, bytes, &s_bar[s]);
+      bulk_g2s(s_x[s], tokens + abs, bytes, &s_bar[s]);
+    }
     if (++ps.k == ps.nck) {
       ps.k = 0;
       prod_next_unit<CH>(ps, p.us, p.rows, lg, claim);
@@ -208,8 +217,12 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
         if (DIRECT) {
           const uint4* gsrc = reinterpret_cast<const uint4*>(gates + abs) + vi * NV;
           const uint4* xsrc = reinterpret_cast<const uint4*>(tokens + abs) + vi * NV;
+          FPSCAN_DEBUG_ONLY(
+              const bool lok = in_bounds(gsrc, NV * 16, gates, gates + n_el) &&
+                               in_bounds(xsrc, NV * 16, tokens, tokens + n_el);)
 #pragma unroll
           for (int q = 0; q < NV; ++q) {
+            FPSCAN_DEBUG_ONLY(if (!lok) { rg[q] = rx[q] = make_uint4(0, 0, 0, 0); continue; })
             rg[q] = __ldg(gsrc + q);
             rx[q] = __ldg(xsrc + q);
           }
@@ -304,6 +317,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
 #pragma unroll
       for (int i = 0; i < E; ++i) f[REV ? E - 1 - i : i] = yv[i];
       uint4* dst = reinterpret_cast<uint4*>(out + abs) + vi * NV;
+      FPSCAN_DEBUG_ONLY(if (in_bounds(dst, NV * 16, out, out + n_el)))
 #pragma unroll
       for (int q = 0; q < NV; ++q) dst[q] = pack_vec<T>(f + q * V);
     }
@@ -312,7 +326,9 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
       const float new_carry = (row_start && !HAS_INIT) ? cb : fmaf(ca, carry, cb);
       acc_a = (row_start ? 1.f : acc_a) * ca;
       carry = new_carry;
-      if (HAS_CARRY_OUT && tid == 0 && ((REV ? abs : abs + CH) & Lmask) == 0) {
+      if (HAS_CARRY_OUT && tid == 0 && ((REV ? abs : abs + CH) & Lmask) == 0
+          FPSCAN_DEBUG_ONLY(&& in_bounds<4>(p.carry_a + row, 4, p.carry_a, p.carry_a + p.rows)
+                            && in_bounds<4>(p.carry_b + row, 4, p.carry_b, p.carry_b + p.rows))) {
         p.carry_a[row] = acc_a;
         p.carry_b[row] = carry;
       }
@@ -323,7 +339,9 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
           st_relaxed_sys_u64(p.lk.out_word + row, link_word(carry, p.lk.epoch));
         }
       }
-    } else if (HAS_CARRY_OUT && valid && seg_lane_t == tpr - 1) {
+    } else if (HAS_CARRY_OUT && valid && seg_lane_t == tpr - 1
+               FPSCAN_DEBUG_ONLY(&& in_bounds<4>(p.carry_a + row, 4, p.carry_a, p.carry_a + p.rows)
+                                 && in_bounds<4>(p.carry_b + row, 4, p.carry_b, p.carry_b + p.rows))) {
       p.carry_a[row] = pa * a[E - 1];
       p.carry_b[row] = yv[E - 1];
     }

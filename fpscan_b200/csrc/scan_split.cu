@@ -156,12 +156,20 @@ __global__ void __launch_bounds__(kThreads, 3) scan_split_kernel(const SplitKPar
   const int64_t seg = REV ? P - 1 - sp : sp;  // segment index in memory order
   const int64_t base = (row << p.lg) + (seg << (LGCH + 2));  // NC == 4 chunks per segment
 
+  FPSCAN_DEBUG_ONLY(const int64_t n_el = p.rows << p.lg;)  // elements of each tensor
   // Stage the whole segment at once: chunk c (processing order) -> buffer c.
   if (tid == 0) {
     const uint32_t bytes = (uint32_t)(CH * sizeof(T));
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int64_t off = (int64_t)(REV ? NC - 1 - c : c) << LGCH;
+      // debug builds: a copy outside its tensor is skipped, the stage completes
+      FPSCAN_DEBUG_ONLY(
+          if (!in_bounds(gates + base + off, bytes, gates, gates + n_el) ||
+              !in_bounds(tokens + base + off, bytes, tokens, tokens + n_el)) {
+            mbar_arrive(&s_bar[c]);
+            continue;
+          })
       mbar_expect_tx(&s_bar[c], 2u * bytes);
       bulk_g2s(s_g[c], gates + base + off, bytes, &s_bar[c]);
       bulk_g2s(s_x[c], tokens + base + off, bytes, &s_bar[c]);
@@ -252,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 3) scan_split_kernel(const SplitKPar
     for (int i = 0; i < E; ++i)
       f[REV ? E - 1 - i : i] = skip_state ? b[i] : fmaf(a[i], state, b[i]);
     uint4* dst = reinterpret_cast<uint4*>(out + base + off) + vi * NV;
+    FPSCAN_DEBUG_ONLY(if (in_bounds(dst, NV * 16, out, out + n_el)))
 #pragma unroll
     for (int k2 = 0; k2 < NV; ++k2) dst[k2] = pack_vec<T>(f + k2 * V);
     carry = row_start ? cb : fmaf(ca, carry, cb);
@@ -333,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 4) scan_split_bwd_kernel(const Split
   const int64_t base = (row << p.lg) + seg * SE;
   const bool row_end_seg = sp == 0;
   const bool row_start_seg = seg == 0;
+  FPSCAN_DEBUG_ONLY(const int64_t n_el = p.rows << p.lg;)  // elements of each tensor
 
   // Stage everything at once: chunk c (processing order) is memory chunk
   // NC-1-c and completes on barrier c; the gates halo rides with chunk 0,
@@ -345,6 +355,15 @@ __global__ void __launch_bounds__(kThreads, 4) scan_split_bwd_kernel(const Split
       const int64_t off = (int64_t)mc * CH;
       const bool gh = c == 0 && !row_end_seg;
       const bool yh = c == NC - 1 && !row_start_seg;
+      // debug builds: a copy outside its tensor is skipped, the stage completes
+      FPSCAN_DEBUG_ONLY(
+          if (!in_bounds(gates + base + off, bytes + (gh ? 16u : 0u), gates, gates + n_el) ||
+              !in_bounds(gout + base + off, bytes, gout, gout + n_el) ||
+              !in_bounds(yh ? y + base - V : y + base + off, bytes + (yh ? 16u : 0u), y,
+                         y + n_el)) {
+            mbar_arrive(&s_bar[c]);
+            continue;
+          })
       mbar_expect_tx(&s_bar[c], 3u * bytes + (gh ? 16u : 0u) + (yh ? 16u : 0u));
       bulk_g2s(s_g + mc * SV, gates + base + off, bytes + (gh ? 16u : 0u), &s_bar[c]);
       bulk_g2s(s_go + mc * SV, gout + base + off, bytes, &s_bar[c]);
@@ -460,6 +479,8 @@ __global__ void __launch_bounds__(kThreads, 4) scan_split_bwd_kernel(const Split
     const int64_t o = base + (int64_t)mc * CH;
     uint4* d1 = reinterpret_cast<uint4*>(dtok + o) + vi * NV;
     uint4* d2 = reinterpret_cast<uint4*>(dgates + o) + vi * NV;
+    FPSCAN_DEBUG_ONLY(if (in_bounds(d1, NV * 16, dtok, dtok + n_el) &&
+                          in_bounds(d2, NV * 16, dgates, dgates + n_el)))
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       d1[k] = pack_vec<T>(f_dt + k * V);

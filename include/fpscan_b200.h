@@ -316,8 +316,9 @@ FPSCAN_API const char* fpscan_last_error(void);
  * split-row scan gave up waiting for a preceding segment; bit 2: a
  * channel-last CTA found its shared-memory staging buffer misaligned for TMA
  * and skipped its work; bit 3: a chained sequence-sharded scan gave up
- * waiting for a neighbouring rank (fpscan_shard_*_link).  Results of such a
- * launch are not valid.  0 = healthy. */
+ * waiting for a neighbouring rank (fpscan_shard_*_link); bit 4 (16, only in
+ * the bounds-checking build): a kernel skipped a global access outside its
+ * tensor.  Results of such a launch are not valid.  0 = healthy. */
 FPSCAN_API int fpscan_device_status(unsigned* status, int clear);
 
 /* Enqueue on `stream` a read-and-clear of the current device's status word
@@ -336,6 +337,16 @@ FPSCAN_API int fpscan_status_snapshot(unsigned* dst, void* stream);
  * device symbol); set it while no scan runs.  No counterpart in the
  * reference. */
 FPSCAN_API int fpscan_set_wait_limit_ns(uint64_t ns);
+
+/* Test hook of the bounds-checking build (libfpscan_b200_debug.so, built
+ * with -DFPSCAN_DEBUG_BOUNDS: every global access a kernel computes is
+ * checked against its tensor's extent; one outside is skipped and sets
+ * status bit 4).  Returns 1 in that build, 0 in the release build, -1 on a
+ * launch error, after enqueueing on `stream` a probe kernel that, in the
+ * bounds-checking build only, checks (without accessing it) an address just
+ * past an extent -- so that build's status word shows bit 4 afterwards.
+ * No counterpart in the reference. */
+FPSCAN_API int fpscan_debug_bounds(void* stream);
 
 #ifdef __cplusplus
 }
