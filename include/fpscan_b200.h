@@ -10,8 +10,14 @@
  *     elements).  Element type is given by `dtype` (FPSCAN_F32/F16/BF16);
  *     per-row carry buffers are always fp32.
  *   - Work is enqueued asynchronously on `stream` (a cudaStream_t; NULL is
- *     the legacy default stream).  The library never allocates device
- *     memory; calls are re-entrant.  The streaming kernels hand rows to
+ *     the legacy default stream).  No scan, backward or shard call
+ *     allocates device memory (scratch comes from caller workspaces or
+ *     fixed arrays inside the library); the only allocation is the chained
+ *     mode's mailbox, made once by fpscan_link_create.  Calls are
+ *     re-entrant.  Every kernel is launched with programmatic dependent
+ *     launch: its prologue overlaps the previous kernel in the stream, and
+ *     it touches global memory only after that kernel completed.  The
+ *     streaming kernels hand rows to
  *     their CTAs through a counter word that each launch takes from a fixed
  *     array in the library's own device memory (zero between launches), so
  *     launches on different streams may run concurrently, and a launch
