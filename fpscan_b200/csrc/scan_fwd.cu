@@ -396,9 +396,24 @@ static cudaError_t launch_fwd_t(const FwdArgs& a) {
     if (us.ctr == nullptr && us.upr * a.seqlen <= kChunk && !getenv("FPSCAN_B200_NO_DIRECT"))
       return launch_fwd_t<T, NV, REV, HAS_OUT, HAS_INIT, HAS_CARRY_OUT, ACT, true>(a);
   }
-  FwdKParams p{a.gates, a.tokens, a.out, a.init, a.carry_a, a.carry_b, a.rows, us,
+  UnitSched ul = us;
+  if constexpr (DIRECT) {
+    // Direct loads, short rows: pack as many rows per CTA as fill a chunk
+    // (fewer, full CTAs) rather than one short row per CTA with most
+    // threads idle.  FPSCAN_B200_DIRECT_PACK=0 keeps the one-wave tiling.
+    static const bool pack = [] {
+      const char* v = getenv("FPSCAN_B200_DIRECT_PACK");
+      return !(v && v[0] == '0');
+    }();
+    if (pack && a.seqlen < kChunk && ul.upr * a.seqlen < kChunk) {
+      ul.upr = kChunk / a.seqlen;
+      ul.nunits = (a.rows + ul.upr - 1) / ul.upr;
+      ul.grid = ul.nunits;
+    }
+  }
+  FwdKParams p{a.gates, a.tokens, a.out, a.init, a.carry_a, a.carry_b, a.rows, ul,
                ilog2_host(a.seqlen), a.lk};
-  return launch_pdl(kern, (unsigned)us.grid, kThreads, smem, a.stream, p);
+  return launch_pdl(kern, (unsigned)ul.grid, kThreads, smem, a.stream, p);
 }
 
 template <typename T, bool REV, bool HAS_OUT, bool HAS_INIT, bool HAS_CARRY_OUT, int ACT = kActNone>
