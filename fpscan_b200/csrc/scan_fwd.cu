@@ -400,12 +400,16 @@ static cudaError_t launch_fwd_t(const FwdArgs& a) {
   if constexpr (DIRECT) {
     // Direct loads, short rows: pack as many rows per CTA as fill a chunk
     // (fewer, full CTAs) rather than one short row per CTA with most
-    // threads idle.  FPSCAN_B200_DIRECT_PACK=0 keeps the one-wave tiling.
+    // threads idle.  Measured on BASELINE config 2 (512 rows, back-to-back
+    // calls): L = 32 2.00 vs 2.41 us, L = 512 2.60 vs 2.75 us; at L = 1024
+    // (two vectors per thread) 3.26 vs 3.16 us, so rows of 1024 and more
+    // keep one row per CTA.  FPSCAN_B200_DIRECT_PACK=0 keeps the one-wave
+    // tiling everywhere.
     static const bool pack = [] {
       const char* v = getenv("FPSCAN_B200_DIRECT_PACK");
       return !(v && v[0] == '0');
     }();
-    if (pack && a.seqlen < kChunk && ul.upr * a.seqlen < kChunk) {
+    if (pack && a.seqlen <= 512 && a.seqlen < kChunk && ul.upr * a.seqlen < kChunk) {
       ul.upr = kChunk / a.seqlen;
       ul.nunits = (a.rows + ul.upr - 1) / ul.upr;
       ul.grid = ul.nunits;
