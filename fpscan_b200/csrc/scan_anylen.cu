@@ -24,6 +24,8 @@
 // partial vectors are stored element by element.  The last partial vector of
 // the buffer (rows*L not a multiple of the vector width) is not staged by
 // the bulk copies; the one thread that owns it reads it from global memory.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -643,7 +645,20 @@ static cudaError_t launch_one_wave(Kern kern, int smem, const AnyArgs& a, AnyKPa
       occ = 1;
     if (dev >= 0 && dev < 64) occ_cache[dev] = occ;
   }
-  const int64_t slots = (int64_t)a.num_sms * occ;
+  // Tiles: 8 waves' worth of static row tiles, handed out by the block
+  // scheduler as CTAs finish -- the balancing that claimed row units give
+  // the power-of-two kernels, without per-chunk unit bounds in shared
+  // memory (which cost more than they saved here).  Measured (GB/s, fwd /
+  // rev / bwd, one wave -> 8 waves): fp32 (8, 2048, 8191) 5394 / 5584 /
+  // 5492 -> 6563 / 6587 / 5548; bf16 (16, 5120, 16383) 5727 / 5541 / 5434
+  // -> 5858 / 5674 / 5662; fp32 (2, 256, 100000) reverse 4299 -> 4827;
+  // bf16 (8, 2048, 8191) forward 5410 -> 5214 (the one loss).
+  // FPSCAN_B200_ANY_WAVES overrides the number of waves.
+  static const int64_t waves = [] {
+    const char* v = getenv("FPSCAN_B200_ANY_WAVES");
+    return v ? (int64_t)atoi(v) : (int64_t)8;
+  }();
+  const int64_t slots = (int64_t)a.num_sms * occ * (waves > 0 ? waves : 1);
   int64_t rpt = (a.rows + slots - 1) / slots;
   if (rpt < 1) rpt = 1;
   const int64_t tiles = (a.rows + rpt - 1) / rpt;
