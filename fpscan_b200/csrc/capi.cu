@@ -229,6 +229,14 @@ constexpr int64_t kShardMaxL = int64_t(1) << 24;
 
 }  // namespace
 
+bool link_claims() {
+  static const bool on = [] {
+    const char* v = getenv("FPSCAN_B200_LINK_CLAIM");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 bool pdl_enabled() {
   static const bool on = [] {
     const char* v = getenv("FPSCAN_B200_PDL");
@@ -874,7 +882,7 @@ int fpscan_shard_fwd_link(const void* gates, const void* tokens, void* out, floa
   if (prev == nullptr && next == nullptr)
     return fail(FPSCAN_ERR_INVALID, "a linked scan needs an upstream or a downstream rank");
   if (epoch == 0) return fail(FPSCAN_ERR_INVALID, "epoch 0 is reserved");
-  const int nv = 1;  // statically tiled: one vector per thread (measured at config 5)
+  const int nv = 1;  // one vector per thread (measured at config 5)
   const int64_t chunk = (int64_t)kThreads * (16 / dtype_size(dtype)) * nv;
   if (!is_pow2(seqlen) || seqlen <= chunk || seqlen > kShardMaxL)
     return fail(FPSCAN_ERR_INVALID,
@@ -900,6 +908,7 @@ int fpscan_shard_fwd_link(const void* gates, const void* tokens, void* out, floa
     a.lk.out_word = at<uint64_t>(next, m.fwd) + slot;
     a.lk.ack_in = at<uint32_t>(local, m.fwd_ack);
   }
+  a.sched = link_claims() ? sched_counter(a.stream) : nullptr;
   return cuda_result(launch_fwd(a), "fpscan_shard_fwd_link launch");
 }
 
@@ -944,6 +953,7 @@ int fpscan_shard_bwd_link(const void* gates, const void* y, const void* grad_out
     a.lk.out_word = at<uint64_t>(prev, m.bwd) + slot;
     a.lk.ack_in = at<uint32_t>(local, m.bwd_ack);
   }
+  a.sched = link_claims() ? sched_counter(a.stream) : nullptr;
   return cuda_result(launch_bwd(a), "fpscan_shard_bwd_link launch");
 }
 

@@ -197,6 +197,10 @@ struct ClArgs {
 // overlaps the tail of the previous kernel in the stream.
 // FPSCAN_B200_PDL=0 launches without the attribute.
 bool pdl_enabled();
+// Whether the chained (link) kernels claim row units dynamically like the
+// other streaming kernels (default) instead of static row tiles;
+// FPSCAN_B200_LINK_CLAIM=0 gives static tiles.
+bool link_claims();
 template <typename K, typename P>
 cudaError_t launch_pdl(K kern, unsigned grid, unsigned threads, size_t smem, cudaStream_t stream,
                        const P& p) {

@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
   if ((int64_t)blockIdx.x >= p.us.nunits) return;
   // Units and chunk hand-over as in scan_fwd.cu; link variants (always
   // statically tiled) compute their chunk positions in every thread.
-  constexpr bool LOCAL = LINK != 0;
+  constexpr bool LOCAL = false;
   int64_t base0 = 0, n0 = 0, nck0 = 0;
   if constexpr (LOCAL) {
     const int64_t r0 = (int64_t)blockIdx.x * p.us.upr;
@@ -191,21 +191,28 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
     }
 
     // LINK: start the polls this chunk needs (completed after pass 1)
+    // (the polling thread of bit 0 is the producer, which wrote the stage's
+    // position itself; the ack words of bit 1 are read by the threads that
+    // hold a row's first element, once the stage's position is visible)
     uint64_t link_pre = 0;
     uint32_t ack_pre = 0;
-    if constexpr ((LINK & 1) != 0)
-      if (tid == 0 && multi && ((abs + CH) & Lmask) == 0)
-        link_pre = ld_relaxed_sys_u64(p.lk.in_word + (abs >> lg));
-    if constexpr ((LINK & 2) != 0) {
-      const int64_t vs = abs + ((int64_t)vi << LGE);
-      if ((vi << LGE) < cnt && (vs & Lmask) == 0)
-        ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + (vs >> lg));
+    if constexpr ((LINK & 1) != 0) {
+      if (tid == 0 && s_cnt[s] != 0) {
+        const int64_t pabs = s_abs[s];
+        if (multi && ((pabs + CH) & Lmask) == 0)
+          link_pre = ld_relaxed_sys_u64(p.lk.in_word + (pabs >> lg));
+      }
     }
 
     const bool ok = mbar_wait_bounded(&s_bar[s], phase);
     if constexpr (!LOCAL) {
       abs = s_abs[s];
       cnt = s_cnt[s];
+    }
+    if constexpr ((LINK & 2) != 0) {
+      const int64_t vs = abs + ((int64_t)vi << LGE);
+      if ((vi << LGE) < cnt && (vs & Lmask) == 0)
+        ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + (vs >> lg));
     }
     const int64_t vstart = abs + ((int64_t)vi << LGE);  // thread's first element
     const bool valid = (vi << LGE) < cnt;
@@ -260,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
     const int buf = (int)(k & 1);
     if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
     if constexpr ((LINK & 1) != 0) {
-      if (tid == 0 && multi && (((abs + CH) & Lmask) == 0)) {
+      if (tid == 0 && multi && cnt != 0 && (((abs + CH) & Lmask) == 0)) {
         const int64_t lrow = abs >> lg;
         s_link[buf] = link_take(p.lk.in_word + lrow, p.lk.epoch, link_pre);
         st_relaxed_sys_u32(p.lk.ack_out + lrow, p.lk.epoch);  // the slot may be reused
@@ -385,7 +392,8 @@ static cudaError_t launch_bwd_t(const BwdArgs& a) {
   const int64_t slots = (int64_t)a.num_sms * occ;
   constexpr int64_t kChunk = (int64_t)kThreads * Elem<T>::kVec * NV;
   const UnitSched us =
-      plan_units(a.rows, a.seqlen, kChunk, slots, LINK != 0 ? nullptr : a.sched);
+      plan_units(a.rows, a.seqlen, kChunk, slots,
+                 (LINK != 0 && !link_claims()) ? nullptr : a.sched);
   BwdKParams p{a.gates, a.y, a.grad_out, a.dgates, a.dtokens, a.addend, a.y_prev, a.carry_b,
                a.rows, us, ilog2_host(a.seqlen), a.lk};
   return launch_pdl(kern, (unsigned)us.grid, kThreads, smem, a.stream, p);

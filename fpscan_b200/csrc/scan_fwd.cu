@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
   // Chunk positions reach the consumers through s_abs / s_cnt, except in
   // LOCAL variants (direct loads; links, which are always statically tiled),
   // where every thread computes them from its CTA's one tile.
-  constexpr bool LOCAL = DIRECT || LINK != 0;
+  constexpr bool LOCAL = DIRECT;
   int64_t base0 = 0, n0 = 0, nck0 = 0;
   if constexpr (LOCAL) {
     const int64_t r0 = (int64_t)blockIdx.x * p.us.upr;
@@ -192,15 +192,20 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
       cnt = (int)min((int64_t)CH, n0 - off);
     }
 
-    // LINK: start the polls this chunk needs (completed after pass 1)
+    // LINK: start the polls this chunk needs (completed after pass 1).  The
+    // polling thread is the producer, which wrote the stage's position
+    // itself, so it may read it before the stage's copies land.
     uint64_t link_pre = 0;
     uint32_t ack_pre = 0;
-    if constexpr ((LINK & 1) != 0)
-      if (tid == 0 && multi && (abs & Lmask) == 0)
-        link_pre = ld_relaxed_sys_u64(p.lk.in_word + (abs >> lg));
-    if constexpr ((LINK & 2) != 0)
-      if (tid == 0 && ((abs + CH) & Lmask) == 0)
-        ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + (abs >> lg));
+    if constexpr (LINK != 0) {
+      if (tid == 0 && s_cnt[s] != 0) {
+        const int64_t pabs = s_abs[s];
+        if ((LINK & 1) != 0 && multi && (pabs & Lmask) == 0)
+          link_pre = ld_relaxed_sys_u64(p.lk.in_word + (pabs >> lg));
+        if ((LINK & 2) != 0 && ((pabs + CH) & Lmask) == 0)
+          ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + (pabs >> lg));
+      }
+    }
 
     const bool ok = DIRECT || mbar_wait_bounded(&s_bar[s], phase);
     if constexpr (!LOCAL) {
@@ -267,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, (FwdCfg<T, NV>::kMinBlocks)) scan_fw
     const int buf = (int)(k & 1);
     if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
     if constexpr ((LINK & 1) != 0) {
-      if (tid == 0 && multi && ((abs & Lmask) == 0)) {
+      if (tid == 0 && multi && cnt != 0 && ((abs & Lmask) == 0)) {
         const int64_t lrow = abs >> lg;
         const float v = link_take(p.lk.in_word + lrow, p.lk.epoch, link_pre);
         s_link[buf] = v;
@@ -388,7 +393,8 @@ static cudaError_t launch_fwd_t(const FwdArgs& a) {
   // Links keep static tiles (every rank must tile its rows alike); direct
   // loads are for one-chunk tiles only.
   const UnitSched us = plan_units(a.rows, a.seqlen, kChunk, slots,
-                                  (DIRECT || LINK != 0) ? nullptr : a.sched);
+                                  (DIRECT || (LINK != 0 && !link_claims())) ? nullptr
+                                                                            : a.sched);
   // Plain scans whose every tile is a single chunk (one wave of small
   // tiles) run the direct-load variant.
   if constexpr (!DIRECT && LINK == 0 && HAS_OUT && !HAS_INIT && !HAS_CARRY_OUT &&
