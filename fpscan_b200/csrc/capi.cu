@@ -882,8 +882,16 @@ int fpscan_shard_fwd_link(const void* gates, const void* tokens, void* out, floa
   if (prev == nullptr && next == nullptr)
     return fail(FPSCAN_ERR_INVALID, "a linked scan needs an upstream or a downstream rank");
   if (epoch == 0) return fail(FPSCAN_ERR_INVALID, "epoch 0 is reserved");
-  const int nv = 1;  // one vector per thread (measured at config 5)
-  const int64_t chunk = (int64_t)kThreads * (16 / dtype_size(dtype)) * nv;
+  // Two vectors per thread where a row spans more than one such chunk:
+  // measured at config 5 with claimed row units, 2 / 4 GPUs: 12834 / 24973
+  // GB/s against 11615 / 21692 with one.  FPSCAN_B200_LINK_FWD_NV=1 forces
+  // one.
+  static const bool nv_one = [] {
+    const char* v = getenv("FPSCAN_B200_LINK_FWD_NV");
+    return v && v[0] == '1';
+  }();
+  const int64_t chunk = (int64_t)kThreads * (16 / dtype_size(dtype));
+  const int nv = (!nv_one && seqlen > 2 * chunk) ? 2 : 1;
   if (!is_pow2(seqlen) || seqlen <= chunk || seqlen > kShardMaxL)
     return fail(FPSCAN_ERR_INVALID,
                 "linked scan: local seqlen must be a power of 2 > %lld and <= %lld (got %lld)",
