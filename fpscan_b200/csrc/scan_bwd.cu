@@ -15,8 +15,9 @@
 // Pipeline, row-unit scheduling, segmentation of short rows and carry
 // handling follow scan_fwd.cu.  The thread-level scan is two-pass: a thread
 // folds its group into one map before the block scan and re-runs the
-// recurrence from the entering state after it, so no per-element values are
-// live across the barrier.  Optional per-row `addend` (value entering at the row's last
+// recurrence from the entering state after it, so no per-element results
+// are live across the barrier (only the inputs: packed, or for half types at
+// one vector per thread their fp32 conversions, which pass 2 reuses).  Optional per-row `addend` (value entering at the row's last
 // element, i.e. gates[L] * dtokens[L] of the next sequence shard) and
 // `y_prev` (y before the row's first element, from the previous shard) serve
 // the sequence-sharded mode; reduce mode (no outputs) emits per row
@@ -60,8 +61,16 @@ struct BwdKParams {
 // arrives over the link (thread 0 waits, reads, acks, shares through shared
 // memory); bit 1 -- this rank's gates[0]*dtokens[0] of each row goes to the
 // upstream rank.  Link kernels always take y[-1] of each row from y_prev.
+// Half types at one vector per thread keep their fp32 inputs across the
+// barrier; the bound of 4 CTAs per SM holds them at <= 64 registers (62, no
+// spills), where the 4-stage ring also fits 4 CTAs.
+template <typename T, int NV, int ACT>
+constexpr int bwd_min_blocks() {
+  return (sizeof(T) == 2 && NV == 1 && ACT == kActNone) ? 4 : BwdCfg<NV>::kMinBlocks;
+}
+
 template <typename T, int NV, bool HAS_OUT, bool HAS_CARRY, int ACT, int LINK = 0>
-__global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
+__global__ void __launch_bounds__(kThreads, (bwd_min_blocks<T, NV, ACT>()))
     scan_bwd_kernel(const BwdKParams p) {
   constexpr int V = Elem<T>::kVec;
   constexpr int E = V * NV;
@@ -215,15 +224,20 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
         ack_pre = ld_relaxed_sys_u32(p.lk.ack_in + (vs >> lg));
     }
     const int64_t vstart = abs + ((int64_t)vi << LGE);  // thread's first element
-    const bool valid = (vi << LGE) < cnt;
-    const bool grp_row_end = ((vstart + E) & Lmask) == 0;  // holds a row's last element
-    const bool grp_row_first = (vstart & Lmask) == 0;      // holds a row's first element
+    // Rows longer than a chunk come in whole chunks (cnt == CH, or 0 for the
+    // end marker, whose pass 1 is discarded).  Row flags need only the low
+    // 32 bits of the position (seqlen <= 2^24).
+    const bool valid = multi || (vi << LGE) < cnt;
+    const uint32_t vlo = (uint32_t)abs + ((uint32_t)vi << LGE);
+    const uint32_t lmask = (uint32_t)Lmask;
+    const bool grp_row_end = ((vlo + E) & lmask) == 0;  // holds a row's last element
+    const bool grp_row_first = (vlo & lmask) == 0;      // holds a row's first element
 
     Vec16<T> gv[NV], gov[NV], yv[NV];
     float g_next = 1.f, y_before = 0.f;
-    // Two passes over the packed inputs: fold the thread's elements into its
-    // map (ta, tb) now, re-run the recurrence from the entering state after
-    // the block scan (no per-element arrays live across the barrier).
+    // Two passes over the inputs: fold the thread's elements into its map
+    // (ta, tb) now, re-run the recurrence from the entering state after the
+    // block scan (no per-element results live across the barrier).
     float ta = 1.f, tb = 0.f;
     {
       // Halo elements: gates[vstart+E] (first gate of the next slot) and
@@ -250,20 +264,42 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
       if (HAS_OUT && valid && !grp_row_first)
         y_before = Elem<T>::load(reinterpret_cast<const T*>(sy)[-1]);
     }
+    // Half types, one vector, no activation: the converted gates and
+    // grad_out stay in registers for pass 2 instead of the packed vectors.
+    constexpr bool kKeepF = sizeof(T) == 2 && NV == 1 && ACT == kActNone;
+    float cg[kKeepF ? E : 1], cx[kKeepF ? E : 1];
+    if constexpr (kKeepF) {
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        cg[j] = Elem<T>::load(gv[j / V].e[j % V]);
+        cx[j] = Elem<T>::load(gov[j / V].e[j % V]);
+      }
+    }
     if (valid) {
 #pragma unroll
       for (int i = 0; i < E; ++i) {
         const int j = E - 1 - i;  // element within the thread's group, memory order
-        const float g = (j == E - 1) ? g_next
-                                      : act_fwd<ACT, T>(Elem<T>::load(gv[(j + 1) / V].e[(j + 1) % V]));
-        const float x = Elem<T>::load(gov[j / V].e[j % V]);
+        float g, x;
+        if constexpr (kKeepF) {
+          g = (j == E - 1) ? g_next : cg[j + 1];
+          x = cx[j];
+        } else {
+          g = (j == E - 1) ? g_next
+                           : act_fwd<ACT, T>(Elem<T>::load(gv[(j + 1) / V].e[(j + 1) % V]));
+          x = Elem<T>::load(gov[j / V].e[j % V]);
+        }
         ta = i == 0 ? g : ta * g;
         tb = i == 0 ? x : fmaf(tb, g, x);
       }
     }
 
     float pa, pb;
-    warp_exclusive(ta, tb, lane, wwidth, pa, pb);
+    // rows longer than a chunk (the common case): full-warp segments, the
+    // widths fixed at compile time
+    if (multi)
+      warp_exclusive(ta, tb, lane, 32, pa, pb);
+    else
+      warp_exclusive(ta, tb, lane, wwidth, pa, pb);
     const int buf = (int)(k & 1);
     if (lane == 31) s_wt[buf][warp] = make_float2(ta, tb);
     if constexpr ((LINK & 1) != 0) {
@@ -282,9 +318,12 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
     if (tid == 0) issue_next();
 
     float ca = 1.f, cb = 0.f;
-    if (seg_warps >= 2) compose_warp_totals(s_wt[buf], lane, warp, seg_warps, pa, pb, ca, cb);
+    if (multi)
+      compose_warp_totals(s_wt[buf], lane, warp, kWarps, pa, pb, ca, cb);
+    else if (seg_warps >= 2)
+      compose_warp_totals(s_wt[buf], lane, warp, seg_warps, pa, pb, ca, cb);
 
-    const bool row_start = multi ? (((abs + CH) & Lmask) == 0) : true;  // processing order
+    const bool row_start = multi ? ((((uint32_t)abs + CH) & lmask) == 0) : true;  // processing order
     const int64_t row = (multi ? abs : vstart) >> lg;
     float state;
     bool skip_state = false;
@@ -309,37 +348,53 @@ __global__ void __launch_bounds__(kThreads, BwdCfg<NV>::kMinBlocks)
     if (HAS_OUT && valid && grp_row_first)
       yp_first = (HAS_CARRY || LINK != 0) ? p.y_prev[row] : 0.f;
     float d = state;
-    float gcur = g_next;                     // activated gate of element j + 1
-    float f_dt[HAS_OUT ? E : 1], f_dg[HAS_OUT ? E : 1];  // memory order
+    float gcur = g_next;  // activated gate of element j + 1
+    // Each 16-byte vector is packed and stored as soon as its elements are
+    // done, so only one vector's results are live at a time.
+    uint4* d1 = HAS_OUT ? reinterpret_cast<uint4*>(dtok + abs) + vi * NV : nullptr;
+    uint4* d2 = HAS_OUT ? reinterpret_cast<uint4*>(dgates + abs) + vi * NV : nullptr;
+    bool st_ok = valid;
+    FPSCAN_DEBUG_ONLY(if (HAS_OUT) st_ok = st_ok && in_bounds(d1, NV * 16, dtok, dtok + n_el) &&
+                                           in_bounds(d2, NV * 16, dgates, dgates + n_el);)
 #pragma unroll
-    for (int i = 0; i < E; ++i) {
-      const int j = E - 1 - i;
-      const float x = Elem<T>::load(gov[j / V].e[j % V]);
-      d = (i == 0 && skip_state) ? x : fmaf(gcur, d, x);
-      const float gj = act_fwd<ACT, T>(Elem<T>::load(gv[j / V].e[j % V]));
-      if constexpr (HAS_OUT) {
-        const float yp = (j == 0) ? yp_first : Elem<T>::load(yv[(j - 1) / V].e[(j - 1) % V]);
-        f_dt[j] = d;
-        if constexpr (ACT == kActNone)
-          f_dg[j] = d * yp;
-        else
-          f_dg[j] = d * yp * act_grad<ACT>(gj);
+    for (int qq = 0; qq < NV; ++qq) {
+      const int q = NV - 1 - qq;
+      float f_dt[HAS_OUT ? V : 1], f_dg[HAS_OUT ? V : 1];  // memory order within the vector
+#pragma unroll
+      for (int ii = 0; ii < V; ++ii) {
+        const int i = qq * V + ii;
+        const int jv = V - 1 - ii;
+        const int j = q * V + jv;
+        float x, gj;
+        if constexpr (kKeepF) {
+          x = cx[j];
+          gj = cg[j];
+        } else {
+          x = Elem<T>::load(gov[q].e[jv]);
+          gj = act_fwd<ACT, T>(Elem<T>::load(gv[q].e[jv]));
+        }
+        d = (i == 0 && skip_state) ? x : fmaf(gcur, d, x);
+        if constexpr (HAS_OUT) {
+          const float yp = (j == 0) ? yp_first : Elem<T>::load(yv[(j - 1) / V].e[(j - 1) % V]);
+          f_dt[jv] = d;
+          if constexpr (ACT == kActNone)
+            f_dg[jv] = d * yp;
+          else
+            f_dg[jv] = d * yp * act_grad<ACT>(gj);
+        }
+        gcur = gj;
       }
-      gcur = gj;
+      if constexpr (HAS_OUT) {
+        if (st_ok) {
+          d1[q] = pack_vec<T>(f_dt);
+          d2[q] = pack_vec<T>(f_dg);
+        }
+      }
     }
     // now d = dtokens of the group's first element, gcur = its (activated) gate
 
     if (valid) {
       if constexpr (HAS_OUT) {
-        uint4* d1 = reinterpret_cast<uint4*>(dtok + abs) + vi * NV;
-        uint4* d2 = reinterpret_cast<uint4*>(dgates + abs) + vi * NV;
-        FPSCAN_DEBUG_ONLY(if (in_bounds(d1, NV * 16, dtok, dtok + n_el) &&
-                              in_bounds(d2, NV * 16, dgates, dgates + n_el)))
-#pragma unroll
-        for (int q = 0; q < NV; ++q) {
-          d1[q] = pack_vec<T>(f_dt + q * V);
-          d2[q] = pack_vec<T>(f_dg + q * V);
-        }
         if constexpr ((LINK & 2) != 0) {
           if (grp_row_first) {
             const float v = gcur * d;
